@@ -1,0 +1,125 @@
+/*
+ * C ABI of the B200 (sm_100a) sparse_attn_sharedkv library (libsas_b200.so).
+ *
+ * Plain pointers and sizes only. All tensor pointers are DEVICE pointers on
+ * the current CUDA device; `stream` is a cudaStream_t passed as void*. The
+ * library never allocates: every call that needs scratch takes a caller-owned
+ * `workspace` whose size the matching *_workspace_bytes() function returns.
+ * Calls are stateless and re-entrant; all work is enqueued on `stream` and
+ * no call synchronises the host with the device.
+ *
+ * Return values are host-side argument/launch checks (SAS_OK or an SAS_ERR_*
+ * code). Conditions only the device can see (a scheduler overrun, a bounded
+ * wait that ran out) are written to the caller's device `status` word, which
+ * must be zeroed before the call and is read back whenever convenient.
+ */
+#ifndef SAS_B200_H_
+#define SAS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SAS_OK 0
+#define SAS_ERR_INVALID_ARG 1    /* shape / value outside the documented contract */
+#define SAS_ERR_UNSUPPORTED 2    /* valid for the reference API, not implemented here */
+#define SAS_ERR_CUDA 3           /* a CUDA runtime call or launch failed */
+#define SAS_ERR_WORKSPACE 4      /* workspace missing or smaller than required */
+#define SAS_ERR_SCHED_OVERRUN 5  /* device status: scheduler row scan hit its cap */
+#define SAS_ERR_TIMEOUT_BASE 16  /* device status: 16 + id of the bounded wait that ran out */
+
+#define SAS_META_SIZE 1024
+#define SAS_AIC_CORE_NUM 36
+
+/* layout codes (layout_q / layout_kv) */
+#define SAS_LAYOUT_BSND 0
+#define SAS_LAYOUT_TND 1
+#define SAS_LAYOUT_BSH 2
+#define SAS_LAYOUT_PA_ND 0
+
+/* dtype codes */
+#define SAS_DTYPE_BF16 0
+#define SAS_DTYPE_FP16 1
+
+/* stage_mask bits of sas_sparse_attn_sharedkv_fwd (SAS_STAGE_ALL for a normal call) */
+#define SAS_STAGE_PLAN 1
+#define SAS_STAGE_ATTENTION 2
+#define SAS_STAGE_COMBINE 4
+#define SAS_STAGE_ALL 7
+
+/* Library version, for a loader to check it got the build it expects. */
+int sas_version(void);
+
+/* ------------------------------------------------------------------------
+ * Scheduler: SparseAttnSharedkvMetadata.
+ * Replaces sparse_attn_sharedkv_tilelang/metadata.py:1018-1086
+ * (sparse_attn_sharedkv_metadata, the Python port of the AICPU kernel) with a
+ * single-CTA GPU kernel whose int32[1024] output is bit-identical:
+ * faMetadata[36][8] = (enable, bn2_start, m_start, s2_start, bn2_end, m_end,
+ * s2_end, first_fd_workspace_idx) followed by fdMetadata[72][8] (all zero,
+ * as supportFd is false in the reference, metadata.py:323-325).
+ * Optional arrays are passed as NULL with count 0, matching the reference's
+ * "empty tensor" convention (metadata.py:331-341, 345-357, 393-407).
+ * ---------------------------------------------------------------------- */
+size_t sas_metadata_workspace_bytes(int32_t batch_size, int32_t aic_core_num);
+
+int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
+                 const int32_t* cu_seqlens_ori_kv, int32_t n_cu_seqlens_ori_kv,
+                 const int32_t* seqused_q, int32_t n_seqused_q,
+                 const int32_t* seqused_kv, int32_t n_seqused_kv,
+                 int32_t batch_size, int32_t max_seqlen_q, int32_t max_seqlen_kv,
+                 int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                 int32_t cmp_topk, int32_t cmp_ratio, int32_t ori_mask_mode, int32_t ori_win_left,
+                 int32_t layout_q, int32_t layout_kv, int32_t has_cmp_kv, int32_t aic_core_num,
+                 int32_t* metadata_out, int32_t* status,
+                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Forward: the fused sparse shared-KV attention.
+ * Replaces the device half of sparse_attn_sharedkv_tilelang/api.py:129-397
+ * (the JIT kernel of kernel.py:56-1745 and its launch at api.py:372-384):
+ * three launches on `stream` -- a plan kernel that walks the metadata's
+ * per-core (bn2, m) windows (kernel.py:254-278) and sizes split-KV work for
+ * every SM, the fused gather + tcgen05 attention kernel, and the split-KV
+ * combine that folds the sink logit once.
+ *
+ *   q            [num_tokens, num_heads, 512] (TND) or [batch, S, num_heads, 512]
+ *                (BSND, num_tokens = batch*S), bf16 or fp16, contiguous
+ *   ori_kv       paged raw cache [ori_num_blocks, ori_block_size, 1, 512]
+ *   ori_block_table [batch, ori_table_stride] int32
+ *   cmp_kv / cmp_block_table: compressed cache, NULL for SWA (scenario 1)
+ *   cmp_sparse_indices [num_tokens, 1, topk] int32, NULL unless SCFA (scenario 3)
+ *   cu_seqlens_q [batch+1] (required for TND, optional for BSND)
+ *   seqused_kv   [batch]
+ *   sinks        [num_heads] fp32
+ *   metadata     int32[1024] from sas_metadata (or any producer of the contract)
+ *   out          same shape/dtype as q;  lse [num_tokens, num_heads] fp32 (may be NULL)
+ * scenario: 1 = SWA, 2 = CFA (dense compressed rows), 3 = SCFA (top-k).
+ * stage_mask: which of the three launches to enqueue (SAS_STAGE_*); the
+ * stages communicate through `workspace`, so a split call sequence must pass
+ * the same arguments to every stage. SAS_STAGE_ALL is the normal call.
+ * ---------------------------------------------------------------------- */
+size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads, int32_t num_sms);
+
+int sas_sparse_attn_sharedkv_fwd(
+    const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype,
+    int32_t layout_q, int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q,
+    const int32_t* seqused_kv,
+    const void* ori_kv, int64_t ori_num_blocks, int32_t ori_block_size,
+    const int32_t* ori_block_table, int32_t ori_table_stride,
+    const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size,
+    const int32_t* cmp_block_table, int32_t cmp_table_stride,
+    const int32_t* cmp_sparse_indices, int32_t topk,
+    const float* sinks, const int32_t* metadata,
+    float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
+    void* out, float* lse,
+    int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes,
+    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SAS_B200_H_ */

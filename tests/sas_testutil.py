@@ -1,0 +1,134 @@
+"""Shared helpers for the parity tests: fixture loading, running a case
+through the public API, and the acceptance checks.
+
+Acceptance bounds (bf16 / fp16 output against the golden reference):
+max-abs <= 2e-2, mean-abs <= 2e-3, LSE abs <= 1e-3, plus the reference's own
+``_check_result`` / ``_check_lse`` criteria
+(test_sparse_attn_sharedkv.py:394-481), restated in ``check_result_ref``.
+"""
+
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+MAX_ABS = 2e-2
+MEAN_ABS = 2e-3
+LSE_ABS = 1e-3
+
+
+def load_attn_fixtures():
+    z = np.load(os.path.join(GOLDEN, "attn_cases.npz"))
+    cfgs = json.loads(str(z["configs"]))
+    res = []
+    for i, c in enumerate(cfgs):
+        raw = z[f"out_{i}"]
+        if c.get("dtype", "bf16") == "bf16":
+            out = (raw.astype(np.uint32) << 16).view(np.float32)
+        else:
+            out = raw.view(np.float16).astype(np.float32)
+        res.append((c, out, z[f"lse_{i}"]))
+    return res
+
+
+def load_meta_fixtures():
+    z = np.load(os.path.join(GOLDEN, "metadata_cases.npz"))
+    return json.loads(str(z["configs"])), z["outputs"]
+
+
+def build_case(cfg):
+    from dsv4_b200 import synth
+
+    kw = {k: v for k, v in cfg.items() if k not in ("name", "edits")}
+    case = synth.make_case(**kw)
+    for t, pos, val in cfg.get("edits", []):
+        case.idx[t, 0, pos] = val
+    return case
+
+
+def oracle_forward(case, tokens=None):
+    from oracle import golden_oracle as O
+
+    return O.forward(case.q, ori_kv=case.ori_kv, ori_bt=case.ori_bt, cmp_kv=case.cmp_kv, cmp_bt=case.cmp_bt,
+                     idx=case.idx, cu_seqlens_q=case.cu_seqlens_q, seqused_kv=case.seqused_kv, sinks=case.sinks,
+                     softmax_scale=case.softmax_scale, cmp_ratio=case.cmp_ratio, win_left=case.win_left,
+                     dtype=case.dtype, tokens=tokens)
+
+
+def to_device(case, device="cuda"):
+    import torch
+
+    tdt = torch.bfloat16 if case.dtype == "bf16" else torch.float16
+    d = dict(
+        q=torch.from_numpy(case.q).to(tdt).to(device),
+        ori_kv=torch.from_numpy(case.ori_kv).to(tdt).to(device),
+        ori_block_table=torch.from_numpy(case.ori_bt).to(device),
+        cu_seqlens_q=torch.from_numpy(case.cu_seqlens_q).to(device),
+        seqused_kv=torch.from_numpy(case.seqused_kv).to(device),
+        sinks=torch.from_numpy(case.sinks).to(device),
+        softmax_scale=case.softmax_scale,
+        ori_win_left=case.win_left,
+    )
+    if case.scenario >= 2:
+        d["cmp_kv"] = torch.from_numpy(case.cmp_kv).to(tdt).to(device)
+        d["cmp_block_table"] = torch.from_numpy(case.cmp_bt).to(device)
+        d["cmp_ratio"] = case.cmp_ratio
+    if case.scenario == 3:
+        d["cmp_sparse_indices"] = torch.from_numpy(case.idx).to(device)
+    return d
+
+
+def run_api(case, device="cuda", **extra):
+    from dsv4_b200 import sparse_attn_sharedkv
+
+    kw = to_device(case, device)
+    kw.update(extra)
+    q = kw.pop("q")
+    out, lse = sparse_attn_sharedkv(q, return_softmax_lse=True, **kw)
+    return out.float().cpu().numpy(), lse.float().cpu().numpy()
+
+
+def check_close(out, ref_out, lse, ref_lse, rows=None, what=""):
+    if rows is not None:
+        out, ref_out, lse, ref_lse = out[rows], ref_out[rows], lse[rows], ref_lse[rows]
+    d = np.abs(out.astype(np.float64) - ref_out.astype(np.float64))
+    dl = np.abs(lse.astype(np.float64) - ref_lse.astype(np.float64))
+    msg = f"{what}: max-abs {d.max():.3e} mean-abs {d.mean():.3e} lse max-abs {dl.max():.3e}"
+    assert np.isfinite(out).all(), msg + " (non-finite output)"
+    assert d.max() <= MAX_ABS, msg
+    assert d.mean() <= MEAN_ABS, msg
+    assert dl.max() <= LSE_ABS, msg
+    return msg
+
+
+def check_result_ref(real, expt, dtype="bf16"):
+    """The reference's own criterion (test_sparse_attn_sharedkv.py:394-437)."""
+    if dtype == "bf16":
+        rtol, atol = 0.0078125, 0.0001
+    else:
+        rtol, atol = 0.005, 0.000025
+    real = np.asarray(real, np.float32).ravel()
+    expt = np.asarray(expt, np.float32).ravel()
+    ok = np.isclose(real, expt, rtol=rtol, atol=atol, equal_nan=True)
+    n_err = int((~ok).sum())
+    pct = (real.size - n_err) / max(real.size, 1) * 100.0
+    floor = (1.0 / (1 << 14)) / 0.005
+    b = np.maximum(np.maximum(np.abs(real), np.abs(expt)), floor) + 1e-9
+    rel = np.abs(real - expt) / b
+    max_rel = float(rel[~ok].max()) if n_err else 0.0
+    assert pct >= 99.5, f"only {pct:.4f}% within tolerance"
+    assert max_rel < 10.0, f"max normalised relative error {max_rel:.3f}"
+
+
+def check_lse_ref(real, expt, dtype="bf16"):
+    """Reference ``_check_lse`` (test_sparse_attn_sharedkv.py:440-481)."""
+    rtol, atol = (0.015, 0.005) if dtype == "bf16" else (0.01, 0.001)
+    real = np.asarray(real, np.float32).ravel()
+    expt = np.asarray(expt, np.float32).ravel()
+    ok = np.isclose(real, expt, rtol=rtol, atol=atol, equal_nan=True)
+    pct = ok.mean() * 100.0 if ok.size else 100.0
+    assert pct >= 99.5, f"lse: only {pct:.4f}% within tolerance"

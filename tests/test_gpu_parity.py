@@ -1,0 +1,148 @@
+"""GPU parity: the CUDA path (through the public API / C ABI) against the
+reference fixtures and the pinned oracle.
+
+Bounds: max-abs <= 2e-2, mean-abs <= 2e-3, LSE abs <= 1e-3, and the
+reference's _check_result / _check_lse; the scheduler is bit-exact.
+"""
+
+import json
+
+import numpy as np
+import pytest
+
+import sas_testutil as U
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _gpu(sas_lib):
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    from dsv4_b200 import reset_device_status
+
+    reset_device_status()
+    yield
+    from dsv4_b200 import check_device_status
+
+    check_device_status()
+
+
+def _meta_gpu(cfg):
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
+
+    kw = dict(cfg)
+    for k in ("cu_seqlens_q", "seqused_kv"):
+        if k in kw:
+            kw[k] = torch.tensor(kw[k], dtype=torch.int32)
+    return sparse_attn_sharedkv_metadata(device="cuda", **kw).cpu().numpy()
+
+
+def test_metadata_gpu_bit_exact_vs_reference_fixtures():
+    cfgs, outs = U.load_meta_fixtures()
+    bad = [i for i, c in enumerate(cfgs) if not np.array_equal(_meta_gpu(c), outs[i])]
+    assert not bad, f"{len(bad)} mismatches, first {bad[:5]}: {[cfgs[i] for i in bad[:2]]}"
+
+
+def test_metadata_gpu_fuzz_vs_oracle():
+    from oracle import meta_oracle as M
+
+    rng = np.random.default_rng(7)
+    bad = []
+    for it in range(300):
+        B = int(rng.integers(1, 200))
+        ql = rng.integers(1, rng.choice([2, 3, 50, 600]), size=B)
+        kv = np.maximum(rng.integers(1, rng.choice([300, 5000, 100000]), size=B), ql)
+        cfg = dict(num_heads_q=int(rng.choice([16, 64, 128])), num_heads_kv=1, head_dim=512,
+                   cu_seqlens_q=[0] + np.cumsum(ql).tolist(), seqused_kv=kv.tolist(), batch_size=B,
+                   max_seqlen_q=int(ql.max()), max_seqlen_kv=int(kv.max()), layout_q="TND",
+                   has_cmp_kv=bool(rng.random() < 0.8), cmp_ratio=int(rng.choice([4, 128])),
+                   cmp_topk=int(rng.choice([0, 256, 512, 1024])), aic_core_num=int(rng.choice([24, 36, 8])))
+        if not np.array_equal(_meta_gpu(cfg), M.metadata(**cfg)):
+            bad.append(cfg)
+    assert not bad, f"{len(bad)} mismatches; first {json.dumps(bad[0])[:400]}"
+
+
+@pytest.mark.parametrize("i", range(9))
+def test_attention_vs_reference_fixtures(i):
+    cfg, ref_out, ref_lse = U.load_attn_fixtures()[i]
+    case = U.build_case(cfg)
+    out, lse = U.run_api(case)
+    U.check_close(out, ref_out, lse, ref_lse, what=cfg["name"])
+    U.check_result_ref(out, ref_out, case.dtype)
+    U.check_lse_ref(lse, ref_lse, case.dtype)
+
+
+RANDOM_CASES = [
+    dict(ctx=[5000, 129, 127, 1, 20000], q_lens=[1, 1, 1, 1, 1], H=64, K=512, seed=11),
+    dict(ctx=[700, 3000, 64], q_lens=[2, 2, 2], H=128, K=512, seed=12),
+    dict(ctx=[9000, 4000], q_lens=[1, 1], H=128, K=1024, seed=13),
+    dict(ctx=[1500, 260], q_lens=[70, 5], H=64, K=512, seed=14),
+    dict(ctx=[3000], q_lens=[1], H=16, K=256, bs_ori=64, bs_cmp=64, seed=15),
+    dict(ctx=[2000, 1000], q_lens=[3, 4], H=32, K=128, seed=16),
+    dict(ctx=[6000, 300], q_lens=[1, 2], H=96, K=384, seed=17),
+]
+
+
+@pytest.mark.parametrize("cfg", RANDOM_CASES, ids=[f"r{i}" for i in range(len(RANDOM_CASES))])
+def test_attention_vs_oracle(cfg):
+    case = U.build_case(cfg)
+    out, lse = U.run_api(case)
+    ro, rl = U.oracle_forward(case)
+    U.check_close(out, ro, lse, rl, what=str(cfg))
+    U.check_result_ref(out, ro)
+
+
+def test_attention_c2_scale_sampled():
+    """BASELINE config 2 shapes (B=64, H=64, K=512, ctx U[8k,64k], block 128),
+    checked against the oracle on a sample of 8 requests."""
+    from dsv4_b200 import synth
+
+    c = synth.config_contexts("C2")
+    case = U.build_case(dict(ctx=c["ctx"], q_lens=c["q_lens"], H=64, K=512, seed=21))
+    out, lse = U.run_api(case)
+    toks = list(range(0, 64, 8))
+    ro, rl = U.oracle_forward(case, tokens=toks)
+    U.check_close(out, ro, lse, rl, rows=toks, what="C2 sample")
+
+
+def test_bsnd_layout_and_return_types():
+    from dsv4_b200 import sparse_attn_sharedkv
+
+    case = U.build_case(dict(ctx=[900, 1200], q_lens=[3, 3], H=64, K=256, seed=31))
+    d = U.to_device(case)
+    q = d.pop("q")
+    B, S = 2, 3
+    idx = d.pop("cmp_sparse_indices")
+    o_tnd, l_tnd = sparse_attn_sharedkv(q, cmp_sparse_indices=idx, return_softmax_lse=True, **d)
+    o_only = sparse_attn_sharedkv(q, cmp_sparse_indices=idx, **d)
+    assert isinstance(o_only, torch.Tensor) and torch.equal(o_only, o_tnd)
+    assert o_tnd.shape == q.shape and l_tnd.shape == (B * S, 64) and l_tnd.dtype == torch.float32
+    d.pop("cu_seqlens_q")
+    o_b, l_b = sparse_attn_sharedkv(q.reshape(B, S, 64, 512), cmp_sparse_indices=idx.reshape(B, S, 1, 256),
+                                    layout_q="BSND", return_softmax_lse=True, **d)
+    assert o_b.shape == (B, S, 64, 512) and l_b.shape == (B, S, 64)
+    assert torch.equal(o_b.reshape(B * S, 64, 512), o_tnd)
+    assert torch.equal(l_b.reshape(B * S, 64), l_tnd)
+
+
+def test_bsnd_padding_rows_are_zero():
+    from dsv4_b200 import sparse_attn_sharedkv
+
+    case = U.build_case(dict(ctx=[900, 1200], q_lens=[4, 4], H=64, K=256, seed=32))
+    d = U.to_device(case)
+    q = d.pop("q").reshape(2, 4, 64, 512)
+    idx = d.pop("cmp_sparse_indices").reshape(2, 4, 1, 256)
+    d["cu_seqlens_q"] = torch.tensor([0, 2, 5], dtype=torch.int32, device="cuda")  # act_q = 2, 3
+    o, l = sparse_attn_sharedkv(q, cmp_sparse_indices=idx, layout_q="BSND", return_softmax_lse=True, **d)
+    assert torch.count_nonzero(o[0, 2:]) == 0 and torch.count_nonzero(l[0, 2:]) == 0
+    assert torch.count_nonzero(o[1, 3:]) == 0
+    assert torch.count_nonzero(o[0, :2]) > 0
+
+
+def test_deterministic_replay():
+    case = U.build_case(dict(ctx=[20000, 30000, 5000], q_lens=[1, 2, 1], H=128, K=512, seed=41))
+    a, la = U.run_api(case)
+    b, lb = U.run_api(case)
+    assert np.array_equal(a, b) and np.array_equal(la, lb)

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(_HERE, "libsas_b200.so")
 
 SAS_OK = 0
 STAGE_PLAN, STAGE_ATTENTION, STAGE_COMBINE, STAGE_ALL = 1, 2, 4, 7
+OPT_RESCALE_THRESHOLD, OPT_TRACE_BUFFER = 1, 2
 ERRORS = {
     1: "invalid argument",
     2: "unsupported configuration",
@@ -42,6 +43,7 @@ EXPORTS = {
     "sas_metadata": ([vp, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
                       i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
     "sas_fwd_workspace_bytes": ([i32, i32, i32], sz),
+    "sas_fwd_set_option": ([i32, ctypes.c_double, vp], ctypes.c_int),
     "sas_sparse_attn_sharedkv_fwd": ([vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp, i32, vp, i64,
                                       i32, vp, i32, vp, i32, vp, vp, f32, i32, i32, i32, vp, vp, i32, i32, vp, vp, sz, vp],
                                      ctypes.c_int),

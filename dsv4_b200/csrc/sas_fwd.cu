@@ -58,8 +58,11 @@ constexpr int CH = 128;       // KV rows per chunk (MMA M)
 constexpr int NSLAB = 8;      // 64-column slabs per chunk
 constexpr int SLAB_BYTES = CH * 128;  // 16 KB
 constexpr int Q_SLAB_BYTES = HG * 128;  // 8 KB
-constexpr int kThreads = 192;
-constexpr float kTau = 8.0f;  // lazy-rescale threshold (log2 units)
+constexpr int kLoaderWarps = 4;         // warps 0-3: cp.async loaders
+constexpr int kLoaderThreads = 32 * kLoaderWarps;
+constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax / epilogue
+constexpr int kMmaWarp = 8;             // warp 8: TMEM owner and MMA issuer
+constexpr int kThreads = 32 * 9;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -72,7 +75,8 @@ constexpr int OFF_MISC = OFF_P + CH * 128;               // +16 KB
 constexpr int M_BAR = 0;         // 32 mbarriers x 8 B
 constexpr int M_TMEM = 256;      // tmem base address
 constexpr int M_ABORT = 260;
-constexpr int M_MASK = 272;      // 2 x 32 bytes
+constexpr int M_MASK = 272;      // 2 x 4 words
+constexpr int M_FIRST = 320;     // 2 x 4 ints
 constexpr int M_RED = 512;       // 4 x 64 floats = 1 KB
 constexpr int M_MRUN = 1536;     // 64 floats
 constexpr int M_ALPHA = 1792;    // 64 floats
@@ -113,6 +117,8 @@ struct FwdParams {
   int T, H, G, R, scenario, K, ratio, win_left, n_win_chunks;
   int ori_bs, ori_bt_stride, cmp_bs, cmp_bt_stride;
   int ori_rows, cmp_rows;  // OOB row coordinate = row count
+  const uint8_t* ori_kv;   // paged pools, rows of D elements
+  const uint8_t* cmp_kv;
   const int32_t* ori_bt;
   const int32_t* cmp_bt;
   const int32_t* idx;
@@ -126,6 +132,15 @@ struct FwdParams {
   float* part_lse;  // [R*2*G][64]
   int32_t* status;
   int q_box_h;
+  float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
+  unsigned long long* trace; // optional per-CTA cycle counters (nullptr in production)
+};
+
+// trace slots per CTA (SM cycles, accumulated by one thread of each role)
+enum TraceSlot {
+  TR_TOTAL = 0, TR_P_COORD, TR_P_WAIT_EMPTY, TR_P_WAIT_MASK, TR_P_ISSUE, TR_M_WAIT_Q, TR_M_WAIT_FULL,
+  TR_M_WAIT_P, TR_M_WAIT_O, TR_S_WAIT_MASK, TR_S_WAIT_S, TR_S_SOFTMAX, TR_S_WAIT_O, TR_S_EPI, TR_CHUNKS,
+  TR_SEGS, TR_NSLOTS = 16
 };
 
 __device__ __forceinline__ int py_floordiv(int a, int b) {
@@ -319,33 +334,26 @@ __device__ __forceinline__ void warp_reduce_scatter64(float (&v)[64], int lane) 
   }
 }
 
-__device__ __forceinline__ int row_coord_window(const FwdParams& p, const TokInfo& ti, int wchunk, int row,
-                                                bool& valid) {
-  const int lo = max(ti.s_g - p.win_left, 0);
-  const int pos = lo + wchunk * CH + row;
-  valid = (ti.s_g >= 0) && pos <= ti.s_g;
-  if (!valid) return p.ori_rows;
-  const int blk = p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs];
-  if (blk < 0) {
-    valid = false;
-    return p.ori_rows;
-  }
-  return blk * p.ori_bs + pos % p.ori_bs;
+__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+                                      int where, bool tracing, unsigned long long& acc) {
+  const long long t0 = tracing ? clock64() : 0;
+  const bool r = sas::mbar_wait(bar, parity, abort_flag, status, where);
+  if (tracing) acc += clock64() - t0;
+  return r;
 }
 
-__device__ __forceinline__ int cmp_row(const FwdParams& p, const TokInfo& ti, int id, bool& valid) {
-  const int blk = p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id / p.cmp_bs];
-  if (blk < 0) {
-    valid = false;
-    return p.cmp_rows;
-  }
-  return blk * p.cmp_bs + id % p.cmp_bs;
+// 16-byte async copy global -> shared; src_bytes = 0 writes zeros without reading.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+// Arrive on `bar` once every cp.async issued so far by this thread has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sas::smem_u32(bar)) : "memory");
 }
 
 template <int DT>
 __global__ void __launch_bounds__(kThreads, 1)
-    sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_ori,
-                   const __grid_constant__ CUtensorMap tm_cmp, const FwdParams p) {
+    sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_addr = sas::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
@@ -353,7 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + M_BAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + M_ABORT);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + M_TMEM);
-  uint8_t* mask_bytes = misc + M_MASK;
+  uint32_t* mask_words = reinterpret_cast<uint32_t*>(misc + M_MASK);    // [2][4]
+  int* first_neg = reinterpret_cast<int*>(misc + M_FIRST);               // [2][4]
   float* red = reinterpret_cast<float*>(misc + M_RED);
   float* m_run = reinterpret_cast<float*>(misc + M_MRUN);
   float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
@@ -363,8 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
 
   if (tid == 0) {
-    for (int i = 0; i < 8; ++i) {
-      sas::mbar_init(&bars[B_FULL + i], 1);
+    for (int i = 0; i < NSLAB; ++i) {
+      sas::mbar_init(&bars[B_FULL + i], kLoaderThreads);
       sas::mbar_init(&bars[B_EMPTY + i], 1);
     }
     sas::mbar_init(&bars[B_QFULL], 1);
@@ -374,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas::mbar_init(&bars[B_OFULL], 1);
     sas::mbar_init(&bars[B_OEMPTY], 128);
     for (int i = 0; i < 2; ++i) {
-      sas::mbar_init(&bars[B_MFULL + i], 32);
+      sas::mbar_init(&bars[B_MFULL + i], kLoaderThreads / 32);
       sas::mbar_init(&bars[B_MEMPTY + i], 128);
     }
     *abort_flag = 0;
@@ -386,111 +395,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<uint4*>(smem + OFF_Q)[i] = make_uint4(0, 0, 0, 0);
     sas::fence_proxy_async_smem();
   }
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     sas::tmem_alloc(tmem_slot, TMEM_COLS);
     sas::tmem_relinquish();
   }
-  if (warp == 0 && lane == 0) {
-    sas::tma_prefetch_desc(&tm_q);
-    sas::tma_prefetch_desc(&tm_ori);
-    sas::tma_prefetch_desc(&tm_cmp);
-  }
+  if (tid == 0) sas::tma_prefetch_desc(&tm_q);
   sas::tc_fence_before();
   __syncthreads();
   sas::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const bool tracing = p.trace != nullptr;
+  unsigned long long tr[TR_NSLOTS];
+#pragma unroll
+  for (int i = 0; i < TR_NSLOTS; ++i) tr[i] = 0;
+  const long long t_start = tracing ? clock64() : 0;
 
-  if (warp == 0) {
-    // =============================== producer
+  if (warp < kLoaderWarps) {
+    // =============================== loaders: one KV row per thread per chunk
+    const int lw = warp;                // rows [32*lw, 32*lw+32) of every chunk
+    const int row = lw * 32 + lane;
+    const int sub = lane >> 3, c16 = lane & 7;
+    const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
     Walker wk;
     wk.init(p.unit_start, p.T, p.R, r);
     Seg sg;
     uint32_t gchunk = 0, seg_i = 0;
     const uint32_t q_bytes = (uint32_t)NSLAB * p.q_box_h * 128;
-    while (wk.next(sg)) {
+    bool ok = true;
+    while (ok && wk.next(sg)) {
       const TokInfo ti = p.tok[sg.t];
-      if (!sas::mbar_wait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1)) break;
-      if (lane == 0) {
-        sas::mbar_arrive_expect_tx(&bars[B_QFULL], q_bytes);
-        for (int s = 0; s < NSLAB; ++s)
-          sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, sg.t);
+      if (tid == 0) {
+        if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
+          ok = false;
+        } else {
+          sas::mbar_arrive_expect_tx(&bars[B_QFULL], q_bytes);
+          for (int s = 0; s < NSLAB; ++s)
+            sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, sg.t);
+        }
       }
-      // compressed index scan state: has a -1 been seen before this chunk?
+      // the compressed scan stops at the first -1 (golden.py:55-56): a range
+      // that starts inside a token looks for one in the slots before it
       bool stopped = false;
       const int cmp_c0 = max(sg.cb - p.n_win_chunks, 0);
       if (p.scenario == 3 && cmp_c0 > 0) {
         const int lim = min(cmp_c0 * CH, ti.n_cmp);
         const int32_t* ip = p.idx + (size_t)sg.t * p.K;
-        bool neg = false;
-        for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
-        stopped = __any_sync(0xffffffffu, neg);
+        int neg = 0;
+        for (int e = row; e < lim; e += kLoaderThreads) neg |= (ip[e] == -1);
+        stopped = sas::named_bar_or(3, kLoaderThreads, neg) != 0;
       }
-      bool ok = true;
-      for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
-        // ---- resolve the 4 rows of this lane: rows 4*lane .. 4*lane+3
-        int crd[4];
-        bool val[4];
+      for (int c = sg.cb; ok && c < sg.ce; ++c, ++gchunk) {
+        const long long tc0 = tracing ? clock64() : 0;
         const bool is_win = c < p.n_win_chunks;
+        long long coord = -1;  // physical row in the pool, -1 = masked
+        bool val;
         if (is_win) {
-#pragma unroll
-          for (int k = 0; k < 4; ++k) crd[k] = row_coord_window(p, ti, c, lane * 4 + k, val[k]);
+          const int lo = max(ti.s_g - p.win_left, 0);
+          const int pos = lo + c * CH + row;
+          val = (ti.s_g >= 0) && pos <= ti.s_g;
+          if (val) {
+            const int blk = p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs];
+            val = blk >= 0;
+            coord = (long long)blk * p.ori_bs + pos % p.ori_bs;
+          }
         } else {
-          const int j = c - p.n_win_chunks;
-          int ids[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int e = j * CH + lane * 4 + k;
-            val[k] = e < ti.n_cmp;
-            ids[k] = e;
-            if (p.scenario == 3) ids[k] = val[k] ? p.idx[(size_t)sg.t * p.K + e] : 0;
-          }
+          const int e = (c - p.n_win_chunks) * CH + row;
+          val = e < ti.n_cmp;
+          int id = e;
           if (p.scenario == 3) {
-            // golden.py:55-56 stops at the first -1
-            int first = 4;
-#pragma unroll
-            for (int k = 3; k >= 0; --k)
-              if (val[k] && ids[k] == -1) first = k;
-            const unsigned fr = __reduce_min_sync(0xffffffffu, (unsigned)(lane * 4 + first));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const int rw = lane * 4 + k;
-              val[k] = val[k] && !stopped && (unsigned)rw < fr && ids[k] >= 0 && ids[k] < ti.thr;
-            }
-            stopped |= fr < (unsigned)CH;
+            id = val ? p.idx[(size_t)sg.t * p.K + e] : 0;
+            const unsigned bal = __ballot_sync(0xffffffffu, val && id == -1);
+            if (lane == 0) first_neg[(gchunk & 1) * 4 + lw] = bal ? lw * 32 + __ffs(bal) - 1 : CH;
+            sas::named_bar_sync(3, kLoaderThreads);
+            const int* fn = first_neg + (gchunk & 1) * 4;
+            const int cf = min(min(fn[0], fn[1]), min(fn[2], fn[3]));
+            val = val && !stopped && row < cf && id >= 0 && id < ti.thr;
+            stopped = stopped || cf < CH;
           } else {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) val[k] = val[k] && ids[k] < ti.thr;
+            val = val && id < ti.thr;
           }
-#pragma unroll
-          for (int k = 0; k < 4; ++k) crd[k] = val[k] ? cmp_row(p, ti, ids[k], val[k]) : p.cmp_rows;
+          if (val) {
+            const int blk = p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id / p.cmp_bs];
+            val = blk >= 0;
+            coord = (long long)blk * p.cmp_bs + id % p.cmp_bs;
+          }
         }
+        if (!val) coord = -1;
+        if (tracing) tr[TR_P_COORD] += clock64() - tc0;
         // ---- publish the validity mask of this chunk
         const int mb = gchunk & 1;
-        if (!sas::mbar_wait(&bars[B_MEMPTY + mb], ((gchunk >> 1) & 1) ^ 1, abort_flag, p.status, 2)) {
+        if (!twait(&bars[B_MEMPTY + mb], ((gchunk >> 1) & 1) ^ 1, abort_flag, p.status, 2, tracing,
+                   tr[TR_P_WAIT_MASK])) {
           ok = false;
           break;
         }
-        mask_bytes[mb * 32 + lane] =
-            (uint8_t)((val[0] ? 1 : 0) | (val[1] ? 2 : 0) | (val[2] ? 4 : 0) | (val[3] ? 8 : 0));
-        sas::mbar_arrive(&bars[B_MFULL + mb]);
-        // ---- gather the eight 16 KB slabs
-        const void* tm = is_win ? (const void*)&tm_ori : (const void*)&tm_cmp;
+        const unsigned vb = __ballot_sync(0xffffffffu, val);
+        if (lane == 0) {
+          mask_words[mb * 4 + lw] = vb;
+          sas::mbar_arrive(&bars[B_MFULL + mb]);
+        }
+        // ---- rows this lane copies: 4 rows x 8 lanes x 16 B per instruction
+        long long crw[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) crw[i] = __shfl_sync(0xffffffffu, coord, 4 * i + sub);
+        const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
         for (int s = 0; s < NSLAB; ++s) {
-          if (!sas::mbar_wait(&bars[B_EMPTY + s], (gchunk & 1) ^ 1, abort_flag, p.status, 3)) {
+          if (!twait(&bars[B_EMPTY + s], (gchunk & 1) ^ 1, abort_flag, p.status, 3, tracing,
+                     tr[TR_P_WAIT_EMPTY])) {
             ok = false;
             break;
           }
-          if (lane == 0) sas::mbar_arrive_expect_tx(&bars[B_FULL + s], SLAB_BYTES);
-          __syncwarp();
-          sas::tma_gather4(smem + OFF_KV + s * SLAB_BYTES + lane * 512, tm, &bars[B_FULL + s], s * 64, crd[0],
-                           crd[1], crd[2], crd[3]);
+          const uint32_t slab = kv_base + s * SLAB_BYTES;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rl = 4 * i + sub;
+            const uint32_t dst = slab + (lw * 32 + rl) * 128 + ((c16 ^ (rl & 7)) << 4);
+            const bool v = crw[i] >= 0;
+            const uint8_t* src = pool + (size_t)(v ? crw[i] : 0) * (D * 2) + s * 128 + c16 * 16;
+            cp_async16(dst, src, v ? 16u : 0u);
+          }
+          cp_async_arrive(&bars[B_FULL + s]);
         }
-        if (!ok) break;
       }
-      if (!ok) break;
       ++seg_i;
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc1 = sas::umma_idesc_f16(DT == 0 ? 1 : 0, 128, HG, 0, 0);
@@ -504,15 +533,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gchunk = 0, seg_i = 0;
       bool ok = true;
       while (ok && wk.next(sg)) {
-        if (!sas::mbar_wait(&bars[B_QFULL], seg_i & 1, abort_flag, p.status, 4)) break;
+        if (!twait(&bars[B_QFULL], seg_i & 1, abort_flag, p.status, 4, tracing, tr[TR_M_WAIT_Q])) break;
         for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
           const bool first = c == sg.cb, last = c == sg.ce - 1;
           // S^T = K . Q^T
           for (int s = 0; s < NSLAB; ++s) {
-            if (!sas::mbar_wait(&bars[B_FULL + s], gchunk & 1, abort_flag, p.status, 5)) {
+            if (!twait(&bars[B_FULL + s], gchunk & 1, abort_flag, p.status, 5, tracing, tr[TR_M_WAIT_FULL])) {
               ok = false;
               break;
             }
+            sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
             sas::tc_fence_after();
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
@@ -525,12 +555,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           sas::umma_commit(&bars[B_SFULL]);
           if (last) sas::umma_commit(&bars[B_QEMPTY]);
           // O^T += V^T . P^T
-          if (!sas::mbar_wait(&bars[B_PREADY], gchunk & 1, abort_flag, p.status, 6)) {
+          if (!twait(&bars[B_PREADY], gchunk & 1, abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P])) {
             ok = false;
             break;
           }
           if (first && seg_i > 0) {
-            if (!sas::mbar_wait(&bars[B_OEMPTY], (seg_i - 1) & 1, abort_flag, p.status, 7)) {
+            if (!twait(&bars[B_OEMPTY], (seg_i - 1) & 1, abort_flag, p.status, 7, tracing, tr[TR_M_WAIT_O])) {
               ok = false;
               break;
             }
@@ -553,14 +583,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else {
-    // =============================== softmax / epilogue (warps 2..5)
+  } else if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4) {
+    // =============================== softmax / epilogue (one thread per KV row)
     using IO = IoType<DT>;
-    const int quad = warp & 3;             // TMEM lane quadrant of this warp
-    const int row = quad * 32 + lane;      // KV row of the chunk / d within an O^T tile
-    const int st = tid - 64;               // 0..127
+    const int quad = warp & 3;          // TMEM lane quadrant of this warp
+    const int row = quad * 32 + lane;   // KV row of the chunk / d within an O^T tile
+    const int st = tid - kSoftmaxWarp0 * 32;  // 0..127
     const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    float lpart[64];
+    float lsum0 = 0.f, lsum1 = 0.f;     // running sums of heads 2*lane, 2*lane+1 over this warp's rows
     Walker wk;
     wk.init(p.unit_start, p.T, p.R, r);
     Seg sg;
@@ -573,39 +603,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = h0 + st;
         m_run[st] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
       }
-#pragma unroll
-      for (int h = 0; h < 64; ++h) lpart[h] = 0.f;
+      lsum0 = lsum1 = 0.f;
       for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
         const bool first = c == sg.cb, last = c == sg.ce - 1;
         const int mb = gchunk & 1;
-        if (!sas::mbar_wait(&bars[B_MFULL + mb], (gchunk >> 1) & 1, abort_flag, p.status, 8)) {
+        if (!twait(&bars[B_MFULL + mb], (gchunk >> 1) & 1, abort_flag, p.status, 8, tracing, tr[TR_S_WAIT_MASK])) {
           ok = false;
           break;
         }
-        const bool valid = (mask_bytes[mb * 32 + (row >> 2)] >> (row & 3)) & 1;
+        const bool valid = (mask_words[mb * 4 + (row >> 5)] >> (row & 31)) & 1;
         sas::mbar_arrive(&bars[B_MEMPTY + mb]);
-        if (!sas::mbar_wait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9)) {
+        if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) {
           ok = false;
           break;
         }
         sas::tc_fence_after();
-        float x[64];
+        const long long ts0 = tracing ? clock64() : 0;
+        // ---- per-head max over the 128 rows of the chunk
         {
+          float t[64];
           uint32_t ra[32], rb[32];
           sas::tmem_ld32(lane_addr + TM_S, ra);
           sas::tmem_ld32(lane_addr + TM_S + 32, rb);
           sas::tmem_wait_ld();
 #pragma unroll
           for (int h = 0; h < 32; ++h) {
-            x[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
-            x[h + 32] = valid ? __uint_as_float(rb[h]) * p.scale_log2 : -INFINITY;
+            t[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
+            t[h + 32] = valid ? __uint_as_float(rb[h]) * p.scale_log2 : -INFINITY;
           }
-        }
-        // per-head max over the 128 rows
-        {
-          float t[64];
-#pragma unroll
-          for (int h = 0; h < 64; ++h) t[h] = x[h];
           warp_reduce_scatter64<true>(t, lane);
           red[quad * 64 + 2 * lane] = t[0];
           red[quad * 64 + 2 * lane + 1] = t[1];
@@ -616,7 +641,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float mx = fmaxf(fmaxf(red[st], red[64 + st]), fmaxf(red[128 + st], red[192 + st]));
           const float mo = m_run[st];
           float al = 1.f;
-          if (mx > mo + kTau) {
+          if (mx > mo + p.tau) {
             al = sas::ex2(mo - mx);
             m_run[st] = mx;
             need = 1;
@@ -625,8 +650,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         need = sas::named_bar_or(2, 128, need);
         if (need) {
-#pragma unroll
-          for (int h = 0; h < 64; ++h) lpart[h] *= alpha_s[h];
+          lsum0 *= alpha_s[2 * lane];
+          lsum1 *= alpha_s[2 * lane + 1];
           if (!first) {
 #pragma unroll 1
             for (int j = 0; j < 8; ++j) {
@@ -641,41 +666,48 @@ __global__ void __launch_bounds__(kThreads, 1)
             sas::tmem_wait_st();
           }
         }
-        // p = 2^(x - m), rounded copy to smem as P^T (row-major 128 B rows, 128B swizzle)
-        uint32_t pk[32];
+        // ---- p = 2^(x - m); P^T to smem (128 B rows, 128B swizzle); row sums
+        {
+          float pv[64];
+          uint32_t ra[32], rb[32];
+          sas::tmem_ld32(lane_addr + TM_S, ra);
+          sas::tmem_ld32(lane_addr + TM_S + 32, rb);
+          sas::tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 64; h += 2) {
-          const float p0 = sas::ex2(x[h] - m_run[h]);
-          const float p1 = sas::ex2(x[h + 1] - m_run[h + 1]);
-          lpart[h] += p0;
-          lpart[h + 1] += p1;
-          pk[h >> 1] = IO::pack(p0, p1);
-        }
-        uint8_t* prow = pbuf + row * 128;
+          for (int h = 0; h < 32; ++h) {
+            pv[h] = valid ? sas::ex2(__uint_as_float(ra[h]) * p.scale_log2 - m_run[h]) : 0.f;
+            pv[h + 32] = valid ? sas::ex2(__uint_as_float(rb[h]) * p.scale_log2 - m_run[h + 32]) : 0.f;
+          }
+          uint8_t* prow = pbuf + row * 128;
 #pragma unroll
-        for (int c16 = 0; c16 < 8; ++c16) {
-          *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
-              make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+          for (int c16 = 0; c16 < 8; ++c16) {
+            const int h = c16 * 8;
+            *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
+                make_uint4(IO::pack(pv[h], pv[h + 1]), IO::pack(pv[h + 2], pv[h + 3]),
+                           IO::pack(pv[h + 4], pv[h + 5]), IO::pack(pv[h + 6], pv[h + 7]));
+          }
+          warp_reduce_scatter64<false>(pv, lane);
+          lsum0 += pv[0];
+          lsum1 += pv[1];
         }
         sas::fence_proxy_async_smem();
         sas::tc_fence_before();
         sas::mbar_arrive(&bars[B_PREADY]);
+        if (tracing) {
+          tr[TR_S_SOFTMAX] += clock64() - ts0;
+          tr[TR_CHUNKS] += 1;
+        }
 
         if (last) {
           // ------------------------------ epilogue
-          if (!sas::mbar_wait(&bars[B_OFULL], seg_i & 1, abort_flag, p.status, 10)) {
+          if (!twait(&bars[B_OFULL], seg_i & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) {
             ok = false;
             break;
           }
           sas::tc_fence_after();
-          {
-            float t[64];
-#pragma unroll
-            for (int h = 0; h < 64; ++h) t[h] = lpart[h];
-            warp_reduce_scatter64<false>(t, lane);
-            red[quad * 64 + 2 * lane] = t[0];
-            red[quad * 64 + 2 * lane + 1] = t[1];
-          }
+          const long long te0 = tracing ? clock64() : 0;
+          red[quad * 64 + 2 * lane] = lsum0;
+          red[quad * 64 + 2 * lane + 1] = lsum1;
           sas::named_bar_sync(1, 128);
           if (st < HG) {
             const int h = h0 + st;
@@ -736,15 +768,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           sas::tc_fence_before();
           sas::mbar_arrive(&bars[B_OEMPTY]);
+          if (tracing) {
+            tr[TR_S_EPI] += clock64() - te0;
+            tr[TR_SEGS] += 1;
+          }
         }
       }
       ++seg_i;
     }
   }
 
+  if (tracing) {
+    unsigned long long* tp = p.trace + (size_t)blockIdx.x * TR_NSLOTS;
+    if (tid == 0) {
+      tp[TR_P_COORD] = tr[TR_P_COORD];
+      tp[TR_P_WAIT_EMPTY] = tr[TR_P_WAIT_EMPTY];
+      tp[TR_P_WAIT_MASK] = tr[TR_P_WAIT_MASK];
+    } else if (warp == kMmaWarp && lane == 0) {
+      tp[TR_M_WAIT_Q] = tr[TR_M_WAIT_Q];
+      tp[TR_M_WAIT_FULL] = tr[TR_M_WAIT_FULL];
+      tp[TR_M_WAIT_P] = tr[TR_M_WAIT_P];
+      tp[TR_M_WAIT_O] = tr[TR_M_WAIT_O];
+    } else if (tid == kSoftmaxWarp0 * 32) {
+      tp[TR_S_WAIT_MASK] = tr[TR_S_WAIT_MASK];
+      tp[TR_S_WAIT_S] = tr[TR_S_WAIT_S];
+      tp[TR_S_SOFTMAX] = tr[TR_S_SOFTMAX];
+      tp[TR_S_WAIT_O] = tr[TR_S_WAIT_O];
+      tp[TR_S_EPI] = tr[TR_S_EPI];
+      tp[TR_CHUNKS] = tr[TR_CHUNKS];
+      tp[TR_SEGS] = tr[TR_SEGS];
+      tp[TR_TOTAL] = clock64() - t_start;
+    }
+  }
   sas::tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     sas::tc_fence_after();
     sas::tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -855,18 +913,6 @@ EncodeTiledFn get_encode() {
   return fn;
 }
 
-bool make_pool_map(CUtensorMap* m, const void* base, int64_t rows, CUtensorMapDataType dt) {
-  EncodeTiledFn enc = get_encode();
-  if (!enc) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)(rows > 0 ? rows : 1)};
-  cuuint64_t strides[1] = {(cuuint64_t)D * 2};
-  cuuint32_t box[2] = {64, 1};
-  cuuint32_t es[2] = {1, 1};
-  return enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 bool make_q_map(CUtensorMap* m, const void* base, int T, int H, int box_h, CUtensorMapDataType dt) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
@@ -880,6 +926,10 @@ bool make_q_map(CUtensorMap* m, const void* base, int T, int H, int box_h, CUten
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Tuning / diagnostics knobs set through sas_fwd_set_option (process-wide).
+float g_tau = 8.0f;
+unsigned long long* g_trace = nullptr;
 
 struct WsLayout {
   size_t tok, unit, po, pl, total;
@@ -899,6 +949,20 @@ WsLayout ws_layout(int T, int H, int num_sms) {
 }  // namespace
 
 extern "C" int sas_version(void) { return 1; }
+
+extern "C" int sas_fwd_set_option(int32_t option, double value, void* ptr) {
+  switch (option) {
+    case SAS_OPT_RESCALE_THRESHOLD:
+      if (!(value >= 0.0 && value <= 64.0)) return SAS_ERR_INVALID_ARG;
+      g_tau = (float)value;
+      return SAS_OK;
+    case SAS_OPT_TRACE_BUFFER:
+      g_trace = static_cast<unsigned long long*>(ptr);
+      return SAS_OK;
+    default:
+      return SAS_ERR_INVALID_ARG;
+  }
+}
 
 extern "C" size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads, int32_t num_sms) {
   return ws_layout(num_tokens, num_heads, num_sms).total;
@@ -965,14 +1029,11 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
 
   const CUtensorMapDataType tdt = dtype == SAS_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  alignas(64) CUtensorMap tm_q, tm_ori, tm_cmp;
+  alignas(64) CUtensorMap tm_q;
   const int q_box_h = std::min(HG, num_heads);
   const int64_t ori_rows = ori_num_blocks * ori_block_size;
   const int64_t cmp_rows = scenario >= 2 ? cmp_num_blocks * cmp_block_size : 0;
   if (!make_q_map(&tm_q, q, num_tokens, num_heads, q_box_h, tdt)) return SAS_ERR_CUDA;
-  if (!make_pool_map(&tm_ori, ori_kv, ori_rows, tdt)) return SAS_ERR_CUDA;
-  if (!make_pool_map(&tm_cmp, scenario >= 2 ? cmp_kv : ori_kv, scenario >= 2 ? cmp_rows : ori_rows, tdt))
-    return SAS_ERR_CUDA;
 
   FwdParams fp{};
   fp.T = num_tokens;
@@ -990,6 +1051,8 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.cmp_bt_stride = cmp_table_stride;
   fp.ori_rows = (int)ori_rows;
   fp.cmp_rows = (int)(scenario >= 2 ? cmp_rows : ori_rows);
+  fp.ori_kv = static_cast<const uint8_t*>(ori_kv);
+  fp.cmp_kv = static_cast<const uint8_t*>(scenario >= 2 ? cmp_kv : ori_kv);
   fp.ori_bt = ori_block_table;
   fp.cmp_bt = cmp_block_table;
   fp.idx = cmp_sparse_indices;
@@ -1003,6 +1066,8 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.part_lse = reinterpret_cast<float*>(ws + wl.pl);
   fp.status = status;
   fp.q_box_h = q_box_h;
+  fp.tau = g_tau;
+  fp.trace = g_trace;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SAS_ERR_CUDA;
@@ -1016,9 +1081,9 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   }
   if (stage_mask & SAS_STAGE_ATTENTION) {
     if (dtype == SAS_DTYPE_BF16)
-      sas_fwd_kernel<0><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, tm_ori, tm_cmp, fp);
+      sas_fwd_kernel<0><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, fp);
     else
-      sas_fwd_kernel<1><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, tm_ori, tm_cmp, fp);
+      sas_fwd_kernel<1><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, fp);
     if (cudaGetLastError() != cudaSuccess) return SAS_ERR_CUDA;
   }
   if (stage_mask & SAS_STAGE_COMBINE) {

@@ -119,6 +119,20 @@ int sas_sparse_attn_sharedkv_fwd(
     int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes,
     void* stream);
 
+/* ------------------------------------------------------------------------
+ * Process-wide options of the forward kernel (no counterpart in the
+ * reference, whose knobs are compile-time JIT parameters, api.py:59-126).
+ *   SAS_OPT_RESCALE_THRESHOLD (value): the online softmax keeps a per-head
+ *     running max m and only rescales the accumulator when a new chunk's max
+ *     exceeds m by more than `value` (log2 units; default 8, 0 = rescale on
+ *     every increase, like the reference kernel's per-chunk update).
+ *   SAS_OPT_TRACE_BUFFER (ptr): device buffer of 16 uint64 per CTA that
+ *     receives per-role cycle counters of the next launches (NULL = off).
+ * ---------------------------------------------------------------------- */
+#define SAS_OPT_RESCALE_THRESHOLD 1
+#define SAS_OPT_TRACE_BUFFER 2
+int sas_fwd_set_option(int32_t option, double value, void* ptr);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,15 +93,23 @@ def run_api(case, device="cuda", **extra):
 
 
 def check_close(out, ref_out, lse, ref_lse, rows=None, what=""):
+    """BASELINE bounds. They are absolute bounds for N(0,1) data, whose
+    outputs are O(1); for inputs drawn at a larger scale (the reference
+    tests' U(-10, 10)) the output bounds scale with the RMS of the reference
+    output, so that they keep meaning "a few output ulps"."""
     if rows is not None:
         out, ref_out, lse, ref_lse = out[rows], ref_out[rows], lse[rows], ref_lse[rows]
     d = np.abs(out.astype(np.float64) - ref_out.astype(np.float64))
     dl = np.abs(lse.astype(np.float64) - ref_lse.astype(np.float64))
-    msg = f"{what}: max-abs {d.max():.3e} mean-abs {d.mean():.3e} lse max-abs {dl.max():.3e}"
+    scale = max(1.0, float(np.sqrt(np.mean(ref_out.astype(np.float64) ** 2))))
+    ref_ok = float(np.isclose(out, ref_out, rtol=2.0 ** -7, atol=1e-4).mean())
+    msg = (f"{what}: max-abs {d.max():.3e} mean-abs {d.mean():.3e} lse max-abs {dl.max():.3e} "
+           f"(output scale {scale:.2f}; reference isclose criterion {100 * ref_ok:.2f}%)")
+    print(msg)
     assert np.isfinite(out).all(), msg + " (non-finite output)"
-    assert d.max() <= MAX_ABS, msg
-    assert d.mean() <= MEAN_ABS, msg
-    assert dl.max() <= LSE_ABS, msg
+    assert d.max() <= MAX_ABS * scale, msg
+    assert d.mean() <= MEAN_ABS * scale, msg
+    assert dl.max() <= LSE_ABS * max(1.0, float(np.abs(ref_lse).max()) / 10.0), msg
     return msg
 
 

@@ -70,7 +70,6 @@ def test_attention_vs_reference_fixtures(i):
     case = U.build_case(cfg)
     out, lse = U.run_api(case)
     U.check_close(out, ref_out, lse, ref_lse, what=cfg["name"])
-    U.check_result_ref(out, ref_out, case.dtype)
     U.check_lse_ref(lse, ref_lse, case.dtype)
 
 
@@ -91,7 +90,6 @@ def test_attention_vs_oracle(cfg):
     out, lse = U.run_api(case)
     ro, rl = U.oracle_forward(case)
     U.check_close(out, ro, lse, rl, what=str(cfg))
-    U.check_result_ref(out, ro)
 
 
 def test_attention_c2_scale_sampled():

@@ -285,12 +285,17 @@ def cpu_baseline(d, H, K, seconds: float):
     n = max(2, min(T, int(seconds / max(per_tok, 1e-6))))
     case = mini_oracle_case(d, cpu_sample_tokens(cu, n), H, K)
     ntok = case["cu_seqlens_q"][-1]
+    done = 0
     t0 = time.perf_counter()
-    run_oracle(case)
-    dt = time.perf_counter() - t0
-    return {"value": ntok / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"{ntok} of {T} query tokens of the same workload ({dt:.1f} s), numpy restatement of "
-                      f"golden.py with BLAS on all host threads"}
+    while True:
+        run_oracle(case)
+        done += ntok
+        dt = time.perf_counter() - t0
+        if dt >= seconds * 0.9 or done >= 50 * T:
+            break
+    return {"value": done / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{ntok} of {T} query tokens of the same workload, {done // ntok} passes ({dt:.1f} s); "
+                      f"numpy restatement of golden.py (oracle/golden_oracle.py) with BLAS on all host threads"}
 
 
 # ----------------------------------------------------------------- arms
@@ -338,6 +343,7 @@ def ours_arm(a, rank, world, local_rank):
     import torch.distributed as dist
 
     from dsv4_b200 import synth, sparse_attn_sharedkv, check_device_status, _lib
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -387,31 +393,47 @@ def ours_arm(a, rank, world, local_rank):
         dist.barrier()
     torch.cuda.synchronize(dev)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+    def load_for(seconds):
+        # untimed replays of the same step so the clock sampler (100 ms period)
+        # sees the GPU under this load before and after the timed steps
+        t_end = time.perf_counter() + seconds
+        while time.perf_counter() < t_end:
+            for _ in range(50):
+                flush.zero_()
+                replay()
+            torch.cuda.synchronize(dev)
+
     with ClockSampler(local_rank) as clk:
+        load_for(0.4)
         for e0, e1 in evs:
             flush.zero_()
             e0.record(stream)
             replay()
             e1.record(stream)
         torch.cuda.synchronize(dev)
+        load_for(0.4)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
     total_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
     check_device_status(dev)
 
-    # attention kernel alone (the dominant kernel), same stream, flushed L2
-    sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, _stages=_lib.STAGE_PLAN, **d)
-    md = None
+    # attention kernel alone (the dominant kernel), same stream, flushed L2:
+    # metadata and plan computed once, then only the attention launch is timed
+    md = sparse_attn_sharedkv_metadata(
+        num_heads_q=H, num_heads_kv=1, head_dim=512, cu_seqlens_q=d["cu_seqlens_q"], seqused_kv=d["seqused_kv"],
+        batch_size=len(ctx), layout_q="TND", cmp_topk=K, cmp_ratio=4, device=dev)
+    sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, metadata=md, _stages=_lib.STAGE_PLAN,
+                         **d)
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
     for e0, e1 in ev2:
         flush.zero_()
         e0.record(stream)
-        sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, _stages=_lib.STAGE_ATTENTION, **d)
+        sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, metadata=md,
+                             _stages=_lib.STAGE_ATTENTION, **d)
         e1.record(stream)
     torch.cuda.synchronize(dev)
     attn_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev2)
-    _ = md
 
     # e2e through the public API with pinned host inputs / outputs
     host = {}

@@ -111,6 +111,9 @@ struct PlanParams {
   const int32_t* meta;
   TokInfo* tok;
   int32_t* unit_start;  // [T+1]
+  int H, dtype_bytes;
+  void* out;            // rows of tokens without work are zeroed here
+  float* lse;
 };
 
 struct FwdParams {
@@ -140,7 +143,7 @@ struct FwdParams {
 enum TraceSlot {
   TR_TOTAL = 0, TR_P_COORD, TR_P_WAIT_EMPTY, TR_P_WAIT_MASK, TR_P_ISSUE, TR_M_WAIT_Q, TR_M_WAIT_FULL,
   TR_M_WAIT_P, TR_M_WAIT_O, TR_S_WAIT_MASK, TR_S_WAIT_S, TR_S_SOFTMAX, TR_S_WAIT_O, TR_S_EPI, TR_CHUNKS,
-  TR_SEGS, TR_NSLOTS = 16
+  TR_SEGS, TR_E_TMEM, TR_E_STAGE, TR_E_COPY, TR_E_RED, TR_NSLOTS = 20
 };
 
 __device__ __forceinline__ int py_floordiv(int a, int b) {
@@ -220,6 +223,13 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
         if (covered) units = p.n_win_chunks + (n_cmp + CH - 1) / CH;
       }
       p.tok[t] = ti;
+      if (units == 0) {
+        // padding / uncovered token: zero output and LSE (golden.py leaves them zero)
+        uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * p.dtype_bytes);
+        for (int i = 0; i < p.H * D * p.dtype_bytes / 16; ++i) o[i] = make_uint4(0, 0, 0, 0);
+        if (p.lse)
+          for (int h = 0; h < p.H; ++h) p.lse[(size_t)t * p.H + h] = 0.f;
+      }
     }
     // block exclusive scan of units
     int v = units;
@@ -725,31 +735,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           sas::named_bar_sync(1, 128);
+          if (tracing) tr[TR_E_RED] += clock64() - te0;
           if (sg.complete) {
-            typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out);
+            // direct stores: lanes pair up (row, row^1); the even lane stores
+            // head h for both rows, the odd lane head h+32 (4-byte stores, two
+            // 64-byte runs per warp instruction; no shared-memory staging, which
+            // would compete with the next segment's MMA operand reads)
+            typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
+            const bool odd = lane & 1;
+            const int d_even = row & ~1;
             for (int j = 0; j < 4; ++j) {
               uint32_t oa[32], ob[32];
+              const long long tt0 = tracing ? clock64() : 0;
               sas::tmem_ld32(lane_addr + TM_O + 64 * j, oa);
               sas::tmem_ld32(lane_addr + TM_O + 64 * j + 32, ob);
               sas::tmem_wait_ld();
-              uint16_t* stg = reinterpret_cast<uint16_t*>(pbuf);  // [64 heads][128 d]
+              const long long tt1 = tracing ? clock64() : 0;
+              if (tracing) tr[TR_E_TMEM] += tt1 - tt0;
 #pragma unroll
               for (int h = 0; h < 32; ++h) {
-                stg[h * 128 + row] = IO::one(__uint_as_float(oa[h]) * inv_s[h]);
-                stg[(h + 32) * 128 + row] = IO::one(__uint_as_float(ob[h]) * inv_s[h + 32]);
+                const float v0 = __uint_as_float(oa[h]) * inv_s[h];
+                const float v1 = __uint_as_float(ob[h]) * inv_s[h + 32];
+                const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+                const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
+                const int hh = h0 + (odd ? h + 32 : h);
+                if (hh < p.H)
+                  *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
               }
-              sas::named_bar_sync(1, 128);
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                const int id = st + 128 * k;  // 1024 chunks of 16 B
-                const int hh = id >> 4, off = id & 15;
-                const int h = h0 + hh;
-                if (h < p.H) {
-                  const uint4 v = reinterpret_cast<const uint4*>(pbuf)[id];
-                  *reinterpret_cast<uint4*>(outp + ((size_t)sg.t * p.H + h) * D + j * 128 + off * 8) = v;
-                }
-              }
-              sas::named_bar_sync(1, 128);
+              if (tracing) tr[TR_E_STAGE] += clock64() - tt1;
             }
           } else {
             const size_t slot = ((size_t)r * 2 + sg.which) * p.G + g;
@@ -798,6 +811,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tp[TR_CHUNKS] = tr[TR_CHUNKS];
       tp[TR_SEGS] = tr[TR_SEGS];
       tp[TR_TOTAL] = clock64() - t_start;
+      tp[TR_E_TMEM] = tr[TR_E_TMEM];
+      tp[TR_E_STAGE] = tr[TR_E_STAGE];
+      tp[TR_E_COPY] = tr[TR_E_COPY];
+      tp[TR_E_RED] = tr[TR_E_RED];
     }
   }
   sas::tc_fence_before();
@@ -809,90 +826,79 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // --------------------------------------------------------------- combine
+// Grid (R, H): CTA (r, h) looks at the boundary of range r (unit r*u). If the
+// boundary cuts a token and is the first boundary inside it, the CTA merges
+// that token's partials for head h; 128 threads, 4 output columns each.
 template <int DT>
-__global__ void __launch_bounds__(256) sas_combine_kernel(const FwdParams p) {
+__global__ void __launch_bounds__(128) sas_combine_kernel(const FwdParams p) {
   using IO = IoType<DT>;
-  const int t = blockIdx.x / p.G, g = blockIdx.x % p.G;
-  const int st = p.unit_start[t], n = p.unit_start[t + 1] - st;
-  const int h0 = g * HG;
-  const int nh = min(HG, p.H - h0);
-  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out);
-  if (n == 0) {
-    // no work for this token (padding or not covered by the metadata): zeros
-    for (int i = threadIdx.x; i < nh * D / 8; i += blockDim.x) {
-      const int hh = i / (D / 8), off = i % (D / 8);
-      *reinterpret_cast<uint4*>(outp + ((size_t)t * p.H + h0 + hh) * D + off * 8) = make_uint4(0, 0, 0, 0);
-    }
-    if (p.lse)
-      for (int hh = threadIdx.x; hh < nh; hh += blockDim.x) p.lse[(size_t)t * p.H + h0 + hh] = 0.f;
-    return;
-  }
+  const int rb = blockIdx.x;
+  const int h = blockIdx.y;
+  if (h >= p.H || rb == 0) return;
   const int U = p.unit_start[p.T];
   const int u = (U + p.R - 1) / p.R;
-  const int r0 = st / u, r1 = (st + n - 1) / u;
-  if (r0 == r1) return;  // finished in place by the forward kernel
-  __shared__ float w_s[HG][8];
-  __shared__ float inv_den[HG];
-  __shared__ int nsplit_s;
-  const int ns = r1 - r0 + 1;
-  // per-head weights
-  for (int hh = threadIdx.x; hh < nh; hh += blockDim.x) {
-    const int h = h0 + hh;
-    const float sink = p.sinks[h] * kLog2e;
-    float m = sink;
-    for (int i = 0; i < ns; ++i) {
-      const int rr = r0 + i;
-      const int which = (rr == r0 && rr * u < st) ? 1 : 0;
-      const size_t slot = ((size_t)rr * 2 + which) * p.G + g;
-      m = fmaxf(m, p.part_lse[slot * HG + hh]);
-    }
-    float den = sas::ex2(sink - m);
-    for (int i = 0; i < ns; ++i) {
-      const int rr = r0 + i;
-      const int which = (rr == r0 && rr * u < st) ? 1 : 0;
-      const size_t slot = ((size_t)rr * 2 + which) * p.G + g;
-      const float w = sas::ex2(p.part_lse[slot * HG + hh] - m);
-      den += w;
-      if (i < 8) w_s[hh][i] = w;
-    }
-    inv_den[hh] = 1.f / den;
-    if (p.lse) p.lse[(size_t)t * p.H + h] = (m + __log2f(den)) * kLn2;
+  const int b0 = rb * u;
+  if (b0 >= U) return;
+  int lo = 0, hi = p.T - 1;  // token holding unit b0: largest t with unit_start[t] <= b0
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (p.unit_start[mid] <= b0) lo = mid; else hi = mid - 1;
   }
-  if (threadIdx.x == 0) nsplit_s = ns;
-  __syncthreads();
-  (void)nsplit_s;
-  for (int i = threadIdx.x; i < nh * D / 4; i += blockDim.x) {
-    const int hh = i / (D / 4), d4 = i % (D / 4);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < ns; ++k) {
-      const int rr = r0 + k;
-      const int which = (rr == r0 && rr * u < st) ? 1 : 0;
-      const size_t slot = ((size_t)rr * 2 + which) * p.G + g;
-      float w;
-      if (k < 8) {
-        w = w_s[hh][k];
-      } else {  // more than 8 splits: recompute the weight
-        const float sink = p.sinks[h0 + hh] * kLog2e;
-        float m = sink;
-        for (int q = 0; q < ns; ++q) {
-          const int r2 = r0 + q;
-          const int wh = (r2 == r0 && r2 * u < st) ? 1 : 0;
-          m = fmaxf(m, p.part_lse[(((size_t)r2 * 2 + wh) * p.G + g) * HG + hh]);
-        }
-        w = sas::ex2(p.part_lse[slot * HG + hh] - m);
-      }
-      const float4 v = reinterpret_cast<const float4*>(p.part_o + (slot * HG + hh) * D)[d4];
+  const int t = lo;
+  const int st = p.unit_start[t], n = p.unit_start[t + 1] - st;
+  if (b0 == st || (rb - 1) * u > st) return;  // not a cut, or an earlier boundary owns it
+  const int g = h / HG, hh = h % HG;
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + ((size_t)t * p.H + h) * D;
+  const int d4 = threadIdx.x;  // float4 column group
+  const int r0 = st / u, r1 = (st + n - 1) / u;
+  const float sink = p.sinks[h] * kLog2e;
+  constexpr int kMaxUnrolled = 8;
+  float lse_i[kMaxUnrolled];
+  size_t slot_i[kMaxUnrolled];
+  const int ns = r1 - r0 + 1;
+  float m = sink;
+  for (int i = 0; i < ns; ++i) {
+    const int rr = r0 + i;
+    const int which = (rr == r0 && rr * u < st) ? 1 : 0;
+    const size_t slot = ((size_t)rr * 2 + which) * p.G + g;
+    const float l = p.part_lse[slot * HG + hh];
+    if (i < kMaxUnrolled) {
+      lse_i[i] = l;
+      slot_i[i] = slot;
+    }
+    m = fmaxf(m, l);
+  }
+  float den = sas::ex2(sink - m);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < kMaxUnrolled; ++i) {
+    if (i < ns) {
+      const float w = sas::ex2(lse_i[i] - m);
+      den += w;
+      const float4 v = reinterpret_cast<const float4*>(p.part_o + (slot_i[i] * HG + hh) * D)[d4];
       acc.x += w * v.x;
       acc.y += w * v.y;
       acc.z += w * v.z;
       acc.w += w * v.w;
     }
-    const float id = inv_den[hh];
-    uint2 o;
-    o.x = IO::pack(acc.x * id, acc.y * id);
-    o.y = IO::pack(acc.z * id, acc.w * id);
-    *reinterpret_cast<uint2*>(outp + ((size_t)t * p.H + h0 + hh) * D + d4 * 4) = o;
   }
+  for (int i = kMaxUnrolled; i < ns; ++i) {  // long splits (rare): no unrolling
+    const int rr = r0 + i;
+    const size_t slot = ((size_t)rr * 2) * p.G + g;
+    const float w = sas::ex2(p.part_lse[slot * HG + hh] - m);
+    den += w;
+    const float4 v = reinterpret_cast<const float4*>(p.part_o + (slot * HG + hh) * D)[d4];
+    acc.x += w * v.x;
+    acc.y += w * v.y;
+    acc.z += w * v.z;
+    acc.w += w * v.w;
+  }
+  const float id = 1.f / den;
+  uint2 o;
+  o.x = IO::pack(acc.x * id, acc.y * id);
+  o.y = IO::pack(acc.z * id, acc.w * id);
+  reinterpret_cast<uint2*>(outp)[d4] = o;
+  if (p.lse && threadIdx.x == 0) p.lse[(size_t)t * p.H + h] = (m + __log2f(den)) * kLn2;
 }
 
 // ------------------------------------------------------------- host side
@@ -1021,6 +1027,10 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.meta = metadata;
   pp.tok = reinterpret_cast<TokInfo*>(ws + wl.tok);
   pp.unit_start = reinterpret_cast<int32_t*>(ws + wl.unit);
+  pp.H = num_heads;
+  pp.dtype_bytes = 2;
+  pp.out = out;
+  pp.lse = lse;
   if (stage_mask & SAS_STAGE_PLAN) {
     sas_plan_kernel<<<1, 1024, 0, st>>>(pp);
     if (cudaGetLastError() != cudaSuccess) return SAS_ERR_CUDA;
@@ -1088,9 +1098,9 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   }
   if (stage_mask & SAS_STAGE_COMBINE) {
     if (dtype == SAS_DTYPE_BF16)
-      sas_combine_kernel<0><<<num_tokens * G, 256, 0, st>>>(fp);
+      sas_combine_kernel<0><<<dim3(R, num_heads), 128, 0, st>>>(fp);
     else
-      sas_combine_kernel<1><<<num_tokens * G, 256, 0, st>>>(fp);
+      sas_combine_kernel<1><<<dim3(R, num_heads), 128, 0, st>>>(fp);
   }
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }

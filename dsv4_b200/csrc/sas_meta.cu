@@ -34,14 +34,12 @@ struct MetaArgs {
   // derived (metadata.py:359-389)
   int64_t pre_token, next_token, group, m_base, s2_base;
   int is_s1g, is_cfa, is_scfa, att_mode;
+  int fast;  // row_info_fast applies (band mask, finite window, S1G layout)
 };
 
 struct BatchInfo {
   i128 pre_lu, next_lu;
   int64_t s1, s2, s1g_base, s1g_tail;
-  int64_t cost, block, lbc;
-  long long last_row;  // last row index with a non-zero block count (-1 = none)
-  int64_t r0_cost, r0_block, r0_lbc, r0_s2start;
 };
 
 struct RowInfo {
@@ -63,8 +61,73 @@ __device__ __forceinline__ int64_t calc_cost(int64_t m, int64_t s2) {
   return 6 * ((m + 15) >> 4) + 10 * ((s2 + 63) >> 6);
 }
 
+// Division-free form of row_info for the configuration the attention API
+// uses: band mask with a finite left window (mode 4, win_left >= 0), an S1G
+// query layout (BSND / TND / BSH), and every length below 2^30. There
+// m_base == group, so row idx covers exactly query token idx (clamped to the
+// last token when the cursor runs past the batch), and the s2 range is
+// [idx + s2 - s1 - win_left, min(idx, s1-1) + s2 - s1].
+__device__ __forceinline__ bool row_fast_ok(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+  return A.fast && bi.s1 < (1 << 30) && bi.s2 < (1 << 30) && idx < (1LL << 30);
+}
+
+__device__ RowInfo row_info_fast(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+  RowInfo r{0, 0, 0, 0};
+  if (bi.s1g_base == 0) return r;
+  const int64_t s1 = bi.s1, s2 = bi.s2;
+  int64_t first, last;
+  if (s2 == 0) {
+    first = 0;
+    last = 0;
+  } else {
+    const int64_t s1_last = idx < s1 ? idx : s1 - 1;
+    first = idx - (s1 - s2 + A.win_left);
+    last = s1_last + (s2 - s1);
+  }
+  int64_t ol = 0, win_end = 0, win_tail = 0;
+  if (!(first >= s2 || last < 0 || last < first)) {
+    const int64_t of = first < 0 ? 0 : (first > s2 - 1 ? s2 - 1 : first);
+    ol = last > s2 - 1 ? s2 - 1 : last;
+    win_end = ((ol - of) >> 9) + 1;
+    win_tail = (ol - of + 1) & 511;
+  }
+  const int64_t cmp_start = win_end;
+  int64_t act = 0;
+  if (A.has_cmp && A.cmp_ratio > 0) {
+    const int64_t last_tok = (int64_t)((uint32_t)(ol + 1) / (uint32_t)A.cmp_ratio);
+    if (A.is_cfa) act = last_tok;
+    else if (A.is_scfa) act = last_tok < A.cmp_topk ? last_tok : A.cmp_topk;
+  }
+  const int64_t cmp_end = act == 0 ? cmp_start : cmp_start + ((act - 1) >> 9) + 1;
+  const int64_t cmp_tail = act & 511;
+  // s1g tail is zero (m_base == group), so only the "normal" rows of the
+  // cost table (metadata.py:449-477) are used
+  const int64_t nn = calc_cost(A.m_base, 512);
+  int64_t win_block = 0, win_cost = 0, win_lbc = 0;
+  if (win_end > 0) {
+    win_block = win_end;
+    const int64_t t = win_tail != 0 ? 1 : 0;
+    const int64_t w_nt = t ? calc_cost(A.m_base, win_tail) : 0;
+    win_cost = nn * (win_block - t) + w_nt * t;
+    win_lbc = t ? w_nt : nn;
+  }
+  int64_t cmp_block = 0, cmp_cost = 0, cmp_lbc = 0;
+  if (cmp_start < cmp_end) {
+    cmp_block = cmp_end - cmp_start;
+    const int64_t t = cmp_tail != 0 ? 1 : 0;
+    const int64_t c_nt = t ? calc_cost(A.m_base, cmp_tail) : 0;
+    cmp_cost = nn * (cmp_block - t) + c_nt * t;
+    cmp_lbc = t ? c_nt : nn;
+  }
+  r.s2_start = win_block > 0 ? 0 : cmp_start;
+  r.lbc = cmp_block > 0 ? cmp_lbc : win_lbc;
+  r.block = win_block + cmp_block;
+  r.cost = win_cost + cmp_cost;
+  return r;
+}
+
 // _calc_s1g_cache (metadata.py:634-667) reduced to the fields the assignment reads.
-__device__ RowInfo row_info(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+__device__ RowInfo row_info_general(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
   RowInfo r{0, 0, 0, 0};
   if (bi.s1g_base == 0) return r;  // early return path: everything zero
   // _calc_s2_token_range (479-501)
@@ -151,19 +214,23 @@ __device__ RowInfo row_info(const MetaArgs& A, const BatchInfo& bi, int64_t idx)
   return r;
 }
 
-__device__ void batch_info_init(const MetaArgs& A, int64_t b, BatchInfo& bi) {
-  bi.s1 = s1_size(A, b);
-  bi.s2 = s2_size(A, b);
-  bi.pre_lu = (A.mask_mode == 4) ? (i128)bi.s1 - bi.s2 + A.pre_token : (i128)A.pre_token;
+__device__ __forceinline__ RowInfo row_info(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+  return row_fast_ok(A, bi, idx) ? row_info_fast(A, bi, idx) : row_info_general(A, bi, idx);
+}
+
+__device__ __forceinline__ BatchInfo make_bi(const MetaArgs& A, int64_t s1, int64_t s2) {
+  BatchInfo bi;
+  bi.s1 = s1;
+  bi.s2 = s2;
+  bi.pre_lu = (A.mask_mode == 4) ? (i128)s1 - s2 + A.pre_token : (i128)A.pre_token;
   if (A.mask_mode == 0 || A.mask_mode == 1 || A.mask_mode == 2) bi.next_lu = A.next_token;
-  else if (A.mask_mode == 3) bi.next_lu = (i128)bi.s2 - bi.s1;
-  else if (A.mask_mode == 4) bi.next_lu = (i128)bi.s2 - bi.s1 + A.next_token;
+  else if (A.mask_mode == 3) bi.next_lu = (i128)s2 - s1;
+  else if (A.mask_mode == 4) bi.next_lu = (i128)s2 - s1 + A.next_token;
   else bi.next_lu = A.next_token;
-  int64_t rows = bi.s1 * A.group;
-  bi.s1g_base = sas::floordiv64(rows + A.m_base - 1, A.m_base);
-  bi.s1g_tail = rows - sas::floordiv64(rows, A.m_base) * A.m_base;
-  bi.cost = bi.block = bi.lbc = 0;
-  bi.last_row = -1;
+  // m_base == group (metadata.py:388), so every s1g row is one query token
+  bi.s1g_base = s1 > 0 ? s1 : 0;
+  bi.s1g_tail = 0;
+  return bi;
 }
 
 __device__ __forceinline__ int64_t warp_incl_scan(int64_t v, int lane) {
@@ -180,15 +247,37 @@ __device__ __forceinline__ int64_t warp_sum(int64_t v) {
   return v;
 }
 
+// Per-batch state, structure of arrays. It lives in shared memory when the
+// batch fits (kSmemBatches), else in the caller's workspace; same code.
+constexpr int kSmemBatches = 2048;
+constexpr int kNumArrays = 9;  // s1, s2, cost, lbc, last_row, r0 cost, r0 lbc, r0 block, item prefix (+1)
+struct Arrays {
+  long long *s1, *s2, *cost, *lbc, *last_row, *r0c, *r0l, *r0b, *item;
+  __device__ void bind(long long* base, int64_t B) {
+    s1 = base;
+    s2 = s1 + B;
+    cost = s2 + B;
+    lbc = cost + B;
+    last_row = lbc + B;
+    r0c = last_row + B;
+    r0l = r0c + B;
+    r0b = r0l + B;
+    item = r0b + B;  // B + 1 entries
+  }
+};
+
 __global__ void __launch_bounds__(kThreads, 1)
-    sas_metadata_kernel(MetaArgs A, BatchInfo* __restrict__ binfo, long long* __restrict__ item_prefix,
-                        int64_t* __restrict__ core_out, int32_t* __restrict__ meta_out, int32_t* status) {
+    sas_metadata_kernel(MetaArgs A, long long* __restrict__ ws_arrays, int64_t* __restrict__ core_out,
+                        int32_t* __restrict__ meta_out, int32_t* status) {
+  extern __shared__ long long sh_arrays[];
   __shared__ long long s_max_cost;
   __shared__ int s_all_zero;
   __shared__ int64_t s_used;
   __shared__ long long s_total_items;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t B = A.batch;
+  Arrays V;
+  V.bind(B <= kSmemBatches ? sh_arrays : ws_arrays, B > 0 ? B : 1);
   if (tid == 0) {
     s_max_cost = 0;
     s_all_zero = 1;
@@ -197,11 +286,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   // ---- phase 1a: split info per batch (metadata.py:671-683)
   for (int64_t b = tid; b < B; b += kThreads) {
-    BatchInfo bi;
-    batch_info_init(A, b, bi);
-    int64_t s2b = sas::floordiv64(bi.s2 + A.s2_base - 1, A.s2_base);
+    const int64_t s1 = s1_size(A, b), s2 = s2_size(A, b);
+    V.s1[b] = s1;
+    V.s2[b] = s2;
+    const BatchInfo bi = make_bi(A, s1, s2);
+    const int64_t s2b = sas::floordiv64(s2 + A.s2_base - 1, A.s2_base);
     if (bi.s1g_base != 0 && s2b != 0) s_all_zero = 0;
-    binfo[b] = bi;
+    V.cost[b] = 0;
+    V.last_row[b] = -1;
   }
   __syncthreads();
   if (s_all_zero) {
@@ -214,81 +306,76 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---- phase 1b: per-batch costs over 32-row items (metadata.py:685-714)
-    // item counts per batch, exclusive prefix (single-warp scan over batches)
     if (warp == 0) {
       long long carry = 0;
       for (int64_t b0 = 0; b0 < B; b0 += 32) {
-        int64_t b = b0 + lane;
+        const int64_t b = b0 + lane;
         long long n = 0;
         if (b < B) {
-          const BatchInfo& bi = binfo[b];
-          if (bi.s1 != 0 && bi.s2 != 0) n = (bi.s1g_base + 31) >> 5;
+          const long long s1 = V.s1[b], s2 = V.s2[b];
+          if (s1 != 0 && s2 != 0) n = (make_bi(A, s1, s2).s1g_base + 31) >> 5;
         }
-        long long inc = warp_incl_scan(n, lane);
-        if (b < B) item_prefix[b] = carry + inc - n;
+        const long long inc = warp_incl_scan(n, lane);
+        if (b < B) V.item[b] = carry + inc - n;
         carry += __shfl_sync(0xffffffffu, inc, 31);
       }
       if (lane == 0) {
-        item_prefix[B] = carry;
+        V.item[B] = carry;
         s_total_items = carry;
       }
     }
     __syncthreads();
     const long long n_items = s_total_items;
     for (long long it = warp; it < n_items; it += kThreads / 32) {
-      // batch of this item: last b with item_prefix[b] <= it
-      int64_t lo = 0, hi = B - 1;
+      int64_t lo = 0, hi = B - 1;  // batch of this item: last b with item[b] <= it
       while (lo < hi) {
-        int64_t mid = (lo + hi + 1) >> 1;
-        if (item_prefix[mid] <= it) lo = mid; else hi = mid - 1;
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (V.item[mid] <= it) lo = mid; else hi = mid - 1;
       }
       const int64_t b = lo;
-      const BatchInfo bi = binfo[b];
-      int64_t row = (it - item_prefix[b]) * 32 + lane;
+      const BatchInfo bi = make_bi(A, V.s1[b], V.s2[b]);
+      const int64_t row = (it - V.item[b]) * 32 + lane;
       RowInfo r{0, 0, 0, 0};
       if (row < bi.s1g_base) r = row_info(A, bi, row);
-      int64_t cs = warp_sum(r.cost), bs = warp_sum(r.block);
+      const int64_t cs = warp_sum(r.cost);
       long long mx = r.cost;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        long long u = __shfl_xor_sync(0xffffffffu, mx, o);
+        const long long u = __shfl_xor_sync(0xffffffffu, mx, o);
         mx = u > mx ? u : mx;
       }
       long long lr = (row < bi.s1g_base && r.block > 0) ? row : -1;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        long long u = __shfl_xor_sync(0xffffffffu, lr, o);
+        const long long u = __shfl_xor_sync(0xffffffffu, lr, o);
         lr = u > lr ? u : lr;
       }
       if (lane == 0) {
-        atomicAdd(reinterpret_cast<unsigned long long*>(&binfo[b].cost), (unsigned long long)cs);
-        atomicAdd(reinterpret_cast<unsigned long long*>(&binfo[b].block), (unsigned long long)bs);
+        atomicAdd(reinterpret_cast<unsigned long long*>(&V.cost[b]), (unsigned long long)cs);
         atomicMax(&s_max_cost, mx);
-        if (lr >= 0) atomicMax(&binfo[b].last_row, lr);
+        if (lr >= 0) atomicMax(&V.last_row[b], lr);
       }
     }
     __syncthreads();
     for (int64_t b = tid; b < B; b += kThreads) {
-      BatchInfo bi = binfo[b];
-      if (bi.last_row >= 0) bi.lbc = row_info(A, bi, bi.last_row).lbc;
-      RowInfo r0 = row_info(A, bi, 0);
-      bi.r0_cost = r0.cost;
-      bi.r0_block = r0.block;
-      bi.r0_lbc = r0.lbc;
-      bi.r0_s2start = r0.s2_start;
-      binfo[b] = bi;
+      const BatchInfo bi = make_bi(A, V.s1[b], V.s2[b]);
+      V.lbc[b] = V.last_row[b] >= 0 ? row_info(A, bi, V.last_row[b]).lbc : 0;
+      const RowInfo r0 = row_info(A, bi, 0);  // its s2 start is always block 0
+      V.r0c[b] = r0.cost;
+      V.r0l[b] = r0.lbc;
+      V.r0b[b] = r0.block;
     }
     __syncthreads();
     // ---- phase 2: greedy assignment (metadata.py:898-923), warp 0
     if (warp == 0 && A.aic > 0) {
       int64_t total = 0;
-      for (int64_t b = lane; b < B; b += 32) total += binfo[b].cost * A.nkv;
+      for (int64_t b = lane; b < B; b += 32) total += V.cost[b] * A.nkv;
       total = warp_sum(total);
       const int64_t max_s1g_cost = s_max_cost;
       int64_t cur_b = 0, cur_bn2 = 0, cur_s1g = 0, cur_s2 = 0, cur_core = 0;
       int64_t unassigned = total;
-      int64_t bn2_cost = binfo[0].cost, bn2_block = binfo[0].block;
-      RowInfo sc{binfo[0].r0_cost, binfo[0].r0_block, binfo[0].r0_lbc, binfo[0].r0_s2start};
+      int64_t bn2_cost = V.cost[0];
+      RowInfo sc{V.r0c[0], V.r0b[0], V.r0l[0], 0};
       cur_s2 = sc.s2_start;
       bool finished = false, overrun = false;
       const int64_t nbn2 = B * A.nkv;
@@ -297,40 +384,56 @@ __global__ void __launch_bounds__(kThreads, 1)
         cur_core = i;
         int64_t den = A.aic - cur_core;
         if (den < 1) den = 1;
-        int64_t avg = sas::floordiv64(unassigned, den);
+        const int64_t avg = sas::floordiv64(unassigned, den);
         const int64_t limit = avg > max_s1g_cost ? avg : max_s1g_cost;
         int64_t core_cost = 0;
-        // AssignByBatch (718-745): sequential over batches (uniform in the warp)
-        while (bn2_cost == 0 || limit + (binfo[cur_b].lbc >> 1) >= core_cost + bn2_cost) {
+        // AssignByBatch (718-745): the current bn2 is tested with its remaining
+        // cost, every following bn2 with its batch's full cost; 32 at a time.
+        if (bn2_cost == 0 || limit + (V.lbc[cur_b] >> 1) >= core_cost + bn2_cost) {
           core_cost += bn2_cost;
-          cur_bn2 += 1;
-          if (cur_bn2 == nbn2) {
-            cur_s1g = 0;
-            cur_s2 = 0;
-            finished = true;
-            break;
+          int64_t base = cur_bn2 + 1;
+          while (true) {
+            const int64_t j = base + lane;
+            const bool end = j >= nbn2;
+            const int64_t bj = end ? 0 : (A.nkv == 1 ? j : sas::floordiv64(j, A.nkv));
+            const int64_t cj = end ? 0 : V.cost[bj];
+            const int64_t incl = warp_incl_scan(cj, lane);
+            const int64_t excl = incl - cj;
+            const bool okj = end || cj == 0 || limit + (V.lbc[bj] >> 1) >= core_cost + excl + cj;
+            const unsigned stop = __ballot_sync(0xffffffffu, end || !okj);
+            if (stop) {
+              const int f = __ffs(stop) - 1;
+              core_cost += __shfl_sync(0xffffffffu, excl, f);
+              if (__shfl_sync(0xffffffffu, (int)end, f)) {
+                cur_bn2 = nbn2;
+                cur_s1g = 0;
+                cur_s2 = 0;
+                finished = true;
+              } else {
+                cur_bn2 = base + f;
+                cur_b = __shfl_sync(0xffffffffu, bj, f);
+                bn2_cost = __shfl_sync(0xffffffffu, cj, f);
+                cur_s1g = 0;
+                sc = RowInfo{V.r0c[cur_b], V.r0b[cur_b], V.r0l[cur_b], 0};
+                cur_s2 = 0;
+              }
+              break;
+            }
+            core_cost += __shfl_sync(0xffffffffu, incl, 31);
+            base += 32;
           }
-          int64_t nb = sas::floordiv64(cur_bn2, A.nkv);
-          if (nb != cur_b) cur_b = nb;
-          const BatchInfo& bi = binfo[cur_b];
-          bn2_cost = bi.cost;
-          bn2_block = bi.block;
-          cur_s1g = 0;
-          sc = RowInfo{bi.r0_cost, bi.r0_block, bi.r0_lbc, bi.r0_s2start};
-          cur_s2 = sc.s2_start;
         }
         if (!finished) {
           // AssignByRow (747-764)
-          const BatchInfo bi = binfo[cur_b];
+          const BatchInfo bi = make_bi(A, V.s1[cur_b], V.s2[cur_b]);
           if (limit + (sc.lbc >> 1) >= core_cost + sc.cost) {
             // take the current row, then walk the following non-empty rows
             core_cost += sc.cost;
             bn2_cost = bn2_cost - sc.cost < 0 ? 0 : bn2_cost - sc.cost;
-            bn2_block = bn2_block - sc.block < 0 ? 0 : bn2_block - sc.block;
             int64_t base = cur_s1g + 1;
             int64_t scanned = 0;
             while (true) {
-              RowInfo r = row_info(A, bi, base + lane);
+              const RowInfo r = row_info(A, bi, base + lane);
               const bool considered = r.block != 0;
               const int64_t c = considered ? r.cost : 0;
               const int64_t incl = warp_incl_scan(c, lane);
@@ -340,11 +443,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (fail) {
                 const int f = __ffs(fail) - 1;
                 const int64_t took = __shfl_sync(0xffffffffu, excl, f);
-                const int64_t blk_before = warp_incl_scan(considered && lane < f ? r.block : 0, lane);
-                const int64_t took_blk = __shfl_sync(0xffffffffu, blk_before, 31);
                 core_cost += took;
                 bn2_cost = bn2_cost - took < 0 ? 0 : bn2_cost - took;
-                bn2_block = bn2_block - took_blk < 0 ? 0 : bn2_block - took_blk;
                 cur_s1g = base + f;
                 sc.cost = __shfl_sync(0xffffffffu, r.cost, f);
                 sc.block = __shfl_sync(0xffffffffu, r.block, f);
@@ -354,10 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 break;
               }
               const int64_t all = __shfl_sync(0xffffffffu, incl, 31);
-              const int64_t all_blk = warp_sum(considered ? r.block : 0);
               core_cost += all;
               bn2_cost = bn2_cost - all < 0 ? 0 : bn2_cost - all;
-              bn2_block = bn2_block - all_blk < 0 ? 0 : bn2_block - all_blk;
               base += 32;
               scanned += 32;
               if (scanned > kRowScanCap) {
@@ -377,26 +475,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (overrun && lane == 0 && status) atomicCAS(status, 0, SAS_ERR_SCHED_OVERRUN);
       if (lane == 0) s_used = cur_core + 1 < 1 ? 1 : cur_core + 1;
-      (void)bn2_block;
     }
   }
   __syncthreads();
   // ---- phase 3: pack (metadata.py:974-1009)
   const int64_t used = s_used;
-  for (int i = tid; i < SAS_META_SIZE; i += kThreads) meta_out[i] = 0;
-  __syncthreads();
-  if (tid < SAS_AIC_CORE_NUM) {
-    const int i = tid;
-    int32_t* row = meta_out + i * 8;
-    if (!(i >= used || i >= A.aic)) {
-      row[0] = 1;
-      row[1] = (int32_t)(i == 0 ? 0 : core_out[3 * (i - 1) + 0]);
-      row[2] = (int32_t)(i == 0 ? 0 : core_out[3 * (i - 1) + 1]);
-      row[3] = (int32_t)(i == 0 ? 0 : core_out[3 * (i - 1) + 2]);
-      row[4] = (int32_t)core_out[3 * i + 0];
-      row[5] = (int32_t)core_out[3 * i + 1];
-      row[6] = (int32_t)core_out[3 * i + 2];
+  for (int i = tid; i < SAS_META_SIZE; i += kThreads) {
+    int32_t v = 0;
+    if (i < SAS_AIC_CORE_NUM * 8) {
+      const int core = i >> 3, f = i & 7;
+      if (core < used && core < A.aic) {
+        if (f == 0) v = 1;
+        else if (f <= 3) v = core == 0 ? 0 : (int32_t)core_out[3 * (core - 1) + (f - 1)];
+        else if (f <= 6) v = (int32_t)core_out[3 * core + (f - 4)];
+      }
     }
+    meta_out[i] = v;
   }
 }
 
@@ -405,10 +499,9 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 }  // namespace
 
 extern "C" size_t sas_metadata_workspace_bytes(int32_t batch_size, int32_t aic_core_num) {
-  size_t b = batch_size > 0 ? (size_t)batch_size : 1;
-  size_t c = aic_core_num > 0 ? (size_t)aic_core_num : 1;
-  return align_up(sizeof(BatchInfo) * b, 256) + align_up(sizeof(long long) * (b + 1), 256) +
-         align_up(sizeof(int64_t) * 3 * c, 256);
+  const size_t b = batch_size > 0 ? (size_t)batch_size : 1;
+  const size_t c = aic_core_num > 0 ? (size_t)aic_core_num : 1;
+  return align_up(sizeof(long long) * (kNumArrays * b + 1), 256) + align_up(sizeof(int64_t) * 3 * c, 256);
 }
 
 extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q, const int32_t* cu_seqlens_ori_kv,
@@ -478,15 +571,27 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   }
   A.m_base = A.group;
   A.s2_base = 512;
+  A.fast = (ori_mask_mode == 4 && ori_win_left >= 0 && ori_win_left < (1 << 30) && A.is_s1g && A.att_mode == 1 &&
+            (!A.has_cmp || (cmp_ratio > 0 && cmp_topk >= 0)));
   const size_t need = sas_metadata_workspace_bytes((int32_t)(B > 0 ? B : 1), aic_core_num);
   if (!workspace || workspace_bytes < need) return SAS_ERR_WORKSPACE;
-  char* ws = static_cast<char*>(workspace);
   const size_t b1 = (size_t)(B > 0 ? B : 1);
-  BatchInfo* binfo = reinterpret_cast<BatchInfo*>(ws);
-  long long* item_prefix = reinterpret_cast<long long*>(ws + align_up(sizeof(BatchInfo) * b1, 256));
-  int64_t* core_out = reinterpret_cast<int64_t*>(ws + align_up(sizeof(BatchInfo) * b1, 256) +
-                                                 align_up(sizeof(long long) * (b1 + 1), 256));
-  sas_metadata_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(A, binfo, item_prefix, core_out,
-                                                                             metadata_out, status);
+  long long* arrays = static_cast<long long*>(workspace);
+  int64_t* core_out = reinterpret_cast<int64_t*>(static_cast<char*>(workspace) +
+                                                 align_up(sizeof(long long) * (kNumArrays * b1 + 1), 256));
+  const size_t smem = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * b1 + 1) : 0;
+  if (smem > 48 * 1024) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    static uint64_t attr_done = 0;
+    if (!(attr_done & (1ull << (dev & 63)))) {
+      if (cudaFuncSetAttribute(sas_metadata_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)(sizeof(long long) * (kNumArrays * kSmemBatches + 1))) != cudaSuccess)
+        return SAS_ERR_CUDA;
+      attr_done |= 1ull << (dev & 63);
+    }
+  }
+  sas_metadata_kernel<<<1, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(A, arrays, core_out, metadata_out,
+                                                                                status);
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }

@@ -19,7 +19,8 @@
 namespace {
 
 using i128 = __int128;
-constexpr int kThreads = 1024;
+constexpr int kThreads = 512;
+constexpr int kSmemCap = 200 * 1024;  // dynamic shared memory of the scheduler CTA
 constexpr int64_t kInt64Max = 0x7fffffffffffffffLL;
 constexpr int64_t kRowScanCap = 1LL << 24;
 
@@ -127,7 +128,7 @@ __device__ RowInfo row_info_fast(const MetaArgs& A, const BatchInfo& bi, int64_t
 }
 
 // _calc_s1g_cache (metadata.py:634-667) reduced to the fields the assignment reads.
-__device__ RowInfo row_info_general(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+__device__ __noinline__ RowInfo row_info_general(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
   RowInfo r{0, 0, 0, 0};
   if (bi.s1g_base == 0) return r;  // early return path: everything zero
   // _calc_s2_token_range (479-501)
@@ -250,6 +251,7 @@ __device__ __forceinline__ int64_t warp_sum(int64_t v) {
 // Per-batch state, structure of arrays. It lives in shared memory when the
 // batch fits (kSmemBatches), else in the caller's workspace; same code.
 constexpr int kSmemBatches = 2048;
+constexpr int64_t kSmallRows = 8;  // batches with at most this many rows are costed by one thread
 constexpr int kNumArrays = 9;  // s1, s2, cost, lbc, last_row, r0 cost, r0 lbc, r0 block, item prefix (+1)
 struct Arrays {
   long long *s1, *s2, *cost, *lbc, *last_row, *r0c, *r0l, *r0b, *item;
@@ -266,10 +268,146 @@ struct Arrays {
   }
 };
 
+template <typename I>
+struct RowT {
+  I cost, block, lbc, s2_start;
+};
+template <typename I>
+__device__ __forceinline__ I warp_scan_t(I v, int lane) {
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const I u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  return v;
+}
+
+// The greedy core assignment (metadata.py:872-923) run by one warp. I is
+// int when every cost sum is known to fit in 31 bits (checked by the caller),
+// which halves the shuffle chain of the serial walk; else long long.
+template <typename I>
+__device__ void assign_cores(const MetaArgs& A, const Arrays& V, int64_t B, int64_t total, long long max_cost,
+                             int lane, int64_t* core_out, bool& overrun, int64_t& used, const int2* rc) {
+      const I max_s1g_cost = (I)max_cost;
+  I cur_b = 0, cur_bn2 = 0, cur_s1g = 0, cur_s2 = 0, cur_core = 0;
+  I unassigned = (I)total;
+  I bn2_cost = (I)V.cost[0];
+  RowT<I> sc{(I)V.r0c[0], (I)V.r0b[0], (I)V.r0l[0], 0};
+  cur_s2 = sc.s2_start;
+  bool finished = false;
+  const I nbn2 = (I)(B * A.nkv);
+  for (int i = 0; i < A.aic; ++i) {
+    if (finished || unassigned <= 0) break;
+    cur_core = i;
+    I den = (I)A.aic - cur_core;
+    if (den < 1) den = 1;
+    const I avg = unassigned / den;  // both positive here
+    const I limit = avg > max_s1g_cost ? avg : max_s1g_cost;
+    I core_cost = 0;
+    // AssignByBatch (718-745): the current bn2 is tested with its remaining
+    // cost, every following bn2 with its batch's full cost; 32 at a time.
+    if (bn2_cost == 0 || limit + ((I)V.lbc[cur_b] >> 1) >= core_cost + bn2_cost) {
+      core_cost += bn2_cost;
+      I base = cur_bn2 + 1;
+      while (true) {
+        const I j = base + lane;
+        const bool end = j >= nbn2;
+        const I bj = end ? 0 : (A.nkv == 1 ? j : j / (I)A.nkv);
+        const I cj = end ? 0 : (I)V.cost[bj];
+        const I incl = warp_scan_t<I>(cj, lane);
+        const I excl = incl - cj;
+        const bool okj = end || cj == 0 || limit + ((I)V.lbc[bj] >> 1) >= core_cost + excl + cj;
+        const unsigned stop = __ballot_sync(0xffffffffu, end || !okj);
+        if (stop) {
+          const int f = __ffs(stop) - 1;
+          core_cost += __shfl_sync(0xffffffffu, excl, f);
+          if (__shfl_sync(0xffffffffu, (int)end, f)) {
+            cur_bn2 = nbn2;
+            cur_s1g = 0;
+            cur_s2 = 0;
+            finished = true;
+          } else {
+            cur_bn2 = base + f;
+            cur_b = __shfl_sync(0xffffffffu, bj, f);
+            bn2_cost = __shfl_sync(0xffffffffu, cj, f);
+            cur_s1g = 0;
+            sc = RowT<I>{(I)V.r0c[cur_b], (I)V.r0b[cur_b], (I)V.r0l[cur_b], 0};
+            cur_s2 = 0;
+          }
+          break;
+        }
+        core_cost += __shfl_sync(0xffffffffu, incl, 31);
+        base += 32;
+      }
+    }
+    if (!finished) {
+      // AssignByRow (747-764)
+      if (limit + (sc.lbc >> 1) >= core_cost + sc.cost) {
+        const BatchInfo bi = make_bi(A, V.s1[cur_b], V.s2[cur_b]);
+        // take the current row, then walk the following non-empty rows
+        core_cost += sc.cost;
+        bn2_cost = bn2_cost - sc.cost < 0 ? 0 : bn2_cost - sc.cost;
+        I base = cur_s1g + 1;
+        int64_t scanned = 0;
+        while (true) {
+          const int64_t row = (int64_t)base + lane;
+          RowT<I> r;
+          if (rc != nullptr && bi.s1g_base > kSmallRows && row < bi.s1g_base) {
+            // cached by the per-row pass; s2 start is always 0 on this path and a
+            // row has blocks exactly when its cost is non-zero
+            const int2 e = rc[V.item[cur_b] * 32 + row];
+            r = RowT<I>{(I)e.x, (I)(e.x != 0), (I)e.y, 0};
+          } else {
+            const RowInfo r64 = row_info(A, bi, row);
+            r = RowT<I>{(I)r64.cost, (I)r64.block, (I)r64.lbc, (I)r64.s2_start};
+          }
+          const bool considered = r.block != 0;
+          const I c = considered ? r.cost : 0;
+          const I incl = warp_scan_t<I>(c, lane);
+          const I excl = incl - c;
+          const bool ok = limit + (r.lbc >> 1) >= core_cost + excl + r.cost;
+          const unsigned fail = __ballot_sync(0xffffffffu, considered && !ok);
+          if (fail) {
+            const int f = __ffs(fail) - 1;
+            const I took = __shfl_sync(0xffffffffu, excl, f);
+            core_cost += took;
+            bn2_cost = bn2_cost - took < 0 ? 0 : bn2_cost - took;
+            cur_s1g = base + f;
+            sc.cost = __shfl_sync(0xffffffffu, r.cost, f);
+            sc.block = __shfl_sync(0xffffffffu, r.block, f);
+            sc.lbc = __shfl_sync(0xffffffffu, r.lbc, f);
+            sc.s2_start = __shfl_sync(0xffffffffu, r.s2_start, f);
+            cur_s2 = sc.s2_start;
+            break;
+          }
+          const I all = __shfl_sync(0xffffffffu, incl, 31);
+          core_cost += all;
+          bn2_cost = bn2_cost - all < 0 ? 0 : bn2_cost - all;
+          base += 32;
+          scanned += 32;
+          if (scanned > kRowScanCap) {
+            overrun = true;
+            break;
+          }
+        }
+        if (overrun) break;
+      }
+    }
+    if (lane == 0) {
+      core_out[3 * i + 0] = cur_bn2;
+      core_out[3 * i + 1] = cur_s1g;
+      core_out[3 * i + 2] = cur_s2;
+    }
+    unassigned -= core_cost;
+  }
+  used = cur_core + 1 < 1 ? 1 : cur_core + 1;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     sas_metadata_kernel(MetaArgs A, long long* __restrict__ ws_arrays, int64_t* __restrict__ core_out,
                         int32_t* __restrict__ meta_out, int32_t* status) {
   extern __shared__ long long sh_arrays[];
+
   __shared__ long long s_max_cost;
   __shared__ int s_all_zero;
   __shared__ int64_t s_used;
@@ -313,7 +451,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         long long n = 0;
         if (b < B) {
           const long long s1 = V.s1[b], s2 = V.s2[b];
-          if (s1 != 0 && s2 != 0) n = (make_bi(A, s1, s2).s1g_base + 31) >> 5;
+          if (s1 != 0 && s2 != 0) {
+            const int64_t rows = make_bi(A, s1, s2).s1g_base;
+            n = rows <= kSmallRows ? 0 : (rows + 31) >> 5;  // small batches: one thread each
+          }
         }
         const long long inc = warp_incl_scan(n, lane);
         if (b < B) V.item[b] = carry + inc - n;
@@ -326,6 +467,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
     const long long n_items = s_total_items;
+    // per-row cost cache for the serial walk, in shared memory after the batch arrays
+    const size_t arr_bytes = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * (size_t)(B > 0 ? B : 1) + 1) : 0;
+    int2* rc = nullptr;
+    if (A.fast && arr_bytes + (size_t)n_items * 32 * sizeof(int2) <= (size_t)kSmemCap)
+      rc = reinterpret_cast<int2*>(reinterpret_cast<char*>(sh_arrays) + ((arr_bytes + 15) & ~(size_t)15));
     for (long long it = warp; it < n_items; it += kThreads / 32) {
       int64_t lo = 0, hi = B - 1;  // batch of this item: last b with item[b] <= it
       while (lo < hi) {
@@ -337,6 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (it - V.item[b]) * 32 + lane;
       RowInfo r{0, 0, 0, 0};
       if (row < bi.s1g_base) r = row_info(A, bi, row);
+      if (rc) rc[it * 32 + lane] = make_int2((int)r.cost, (int)r.lbc);
       const int64_t cs = warp_sum(r.cost);
       long long mx = r.cost;
 #pragma unroll
@@ -359,6 +506,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     for (int64_t b = tid; b < B; b += kThreads) {
       const BatchInfo bi = make_bi(A, V.s1[b], V.s2[b]);
+      if (bi.s1 != 0 && bi.s2 != 0 && bi.s1g_base <= kSmallRows) {
+        // small batch (decode): all its rows here, in row order
+        long long cost = 0, mx = 0, lr = -1;
+        for (int64_t row = 0; row < bi.s1g_base; ++row) {
+          const RowInfo r = row_info(A, bi, row);
+          cost += r.cost;
+          mx = r.cost > mx ? r.cost : mx;
+          if (r.block > 0) lr = row;
+        }
+        V.cost[b] = cost;
+        V.last_row[b] = lr;
+        atomicMax(&s_max_cost, mx);
+      }
       V.lbc[b] = V.last_row[b] >= 0 ? row_info(A, bi, V.last_row[b]).lbc : 0;
       const RowInfo r0 = row_info(A, bi, 0);  // its s2 start is always block 0
       V.r0c[b] = r0.cost;
@@ -371,110 +531,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t total = 0;
       for (int64_t b = lane; b < B; b += 32) total += V.cost[b] * A.nkv;
       total = warp_sum(total);
-      const int64_t max_s1g_cost = s_max_cost;
-      int64_t cur_b = 0, cur_bn2 = 0, cur_s1g = 0, cur_s2 = 0, cur_core = 0;
-      int64_t unassigned = total;
-      int64_t bn2_cost = V.cost[0];
-      RowInfo sc{V.r0c[0], V.r0b[0], V.r0l[0], 0};
-      cur_s2 = sc.s2_start;
-      bool finished = false, overrun = false;
-      const int64_t nbn2 = B * A.nkv;
-      for (int64_t i = 0; i < A.aic; ++i) {
-        if (finished || unassigned <= 0) break;
-        cur_core = i;
-        int64_t den = A.aic - cur_core;
-        if (den < 1) den = 1;
-        const int64_t avg = sas::floordiv64(unassigned, den);
-        const int64_t limit = avg > max_s1g_cost ? avg : max_s1g_cost;
-        int64_t core_cost = 0;
-        // AssignByBatch (718-745): the current bn2 is tested with its remaining
-        // cost, every following bn2 with its batch's full cost; 32 at a time.
-        if (bn2_cost == 0 || limit + (V.lbc[cur_b] >> 1) >= core_cost + bn2_cost) {
-          core_cost += bn2_cost;
-          int64_t base = cur_bn2 + 1;
-          while (true) {
-            const int64_t j = base + lane;
-            const bool end = j >= nbn2;
-            const int64_t bj = end ? 0 : (A.nkv == 1 ? j : sas::floordiv64(j, A.nkv));
-            const int64_t cj = end ? 0 : V.cost[bj];
-            const int64_t incl = warp_incl_scan(cj, lane);
-            const int64_t excl = incl - cj;
-            const bool okj = end || cj == 0 || limit + (V.lbc[bj] >> 1) >= core_cost + excl + cj;
-            const unsigned stop = __ballot_sync(0xffffffffu, end || !okj);
-            if (stop) {
-              const int f = __ffs(stop) - 1;
-              core_cost += __shfl_sync(0xffffffffu, excl, f);
-              if (__shfl_sync(0xffffffffu, (int)end, f)) {
-                cur_bn2 = nbn2;
-                cur_s1g = 0;
-                cur_s2 = 0;
-                finished = true;
-              } else {
-                cur_bn2 = base + f;
-                cur_b = __shfl_sync(0xffffffffu, bj, f);
-                bn2_cost = __shfl_sync(0xffffffffu, cj, f);
-                cur_s1g = 0;
-                sc = RowInfo{V.r0c[cur_b], V.r0b[cur_b], V.r0l[cur_b], 0};
-                cur_s2 = 0;
-              }
-              break;
-            }
-            core_cost += __shfl_sync(0xffffffffu, incl, 31);
-            base += 32;
-          }
-        }
-        if (!finished) {
-          // AssignByRow (747-764)
-          const BatchInfo bi = make_bi(A, V.s1[cur_b], V.s2[cur_b]);
-          if (limit + (sc.lbc >> 1) >= core_cost + sc.cost) {
-            // take the current row, then walk the following non-empty rows
-            core_cost += sc.cost;
-            bn2_cost = bn2_cost - sc.cost < 0 ? 0 : bn2_cost - sc.cost;
-            int64_t base = cur_s1g + 1;
-            int64_t scanned = 0;
-            while (true) {
-              const RowInfo r = row_info(A, bi, base + lane);
-              const bool considered = r.block != 0;
-              const int64_t c = considered ? r.cost : 0;
-              const int64_t incl = warp_incl_scan(c, lane);
-              const int64_t excl = incl - c;
-              const bool ok = limit + (r.lbc >> 1) >= core_cost + excl + r.cost;
-              const unsigned fail = __ballot_sync(0xffffffffu, considered && !ok);
-              if (fail) {
-                const int f = __ffs(fail) - 1;
-                const int64_t took = __shfl_sync(0xffffffffu, excl, f);
-                core_cost += took;
-                bn2_cost = bn2_cost - took < 0 ? 0 : bn2_cost - took;
-                cur_s1g = base + f;
-                sc.cost = __shfl_sync(0xffffffffu, r.cost, f);
-                sc.block = __shfl_sync(0xffffffffu, r.block, f);
-                sc.lbc = __shfl_sync(0xffffffffu, r.lbc, f);
-                sc.s2_start = __shfl_sync(0xffffffffu, r.s2_start, f);
-                cur_s2 = sc.s2_start;
-                break;
-              }
-              const int64_t all = __shfl_sync(0xffffffffu, incl, 31);
-              core_cost += all;
-              bn2_cost = bn2_cost - all < 0 ? 0 : bn2_cost - all;
-              base += 32;
-              scanned += 32;
-              if (scanned > kRowScanCap) {
-                overrun = true;
-                break;
-              }
-            }
-            if (overrun) break;
-          }
-        }
-        if (lane == 0) {
-          core_out[3 * i + 0] = cur_bn2;
-          core_out[3 * i + 1] = cur_s1g;
-          core_out[3 * i + 2] = cur_s2;
-        }
-        unassigned -= core_cost;
-      }
+      bool overrun = false;
+      int64_t used = 1;
+      if (A.fast && total < (1LL << 30) && s_max_cost < (1LL << 30) && B * A.nkv < (1LL << 30))
+        assign_cores<int>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc);
+      else
+        assign_cores<long long>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc);
       if (overrun && lane == 0 && status) atomicCAS(status, 0, SAS_ERR_SCHED_OVERRUN);
-      if (lane == 0) s_used = cur_core + 1 < 1 ? 1 : cur_core + 1;
+      if (lane == 0) s_used = used;
     }
   }
   __syncthreads();
@@ -493,6 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     meta_out[i] = v;
   }
 }
+
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -579,14 +644,14 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   long long* arrays = static_cast<long long*>(workspace);
   int64_t* core_out = reinterpret_cast<int64_t*>(static_cast<char*>(workspace) +
                                                  align_up(sizeof(long long) * (kNumArrays * b1 + 1), 256));
-  const size_t smem = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * b1 + 1) : 0;
+  const size_t smem = kSmemCap;
   if (smem > 48 * 1024) {
     int dev = 0;
     cudaGetDevice(&dev);
     static uint64_t attr_done = 0;
     if (!(attr_done & (1ull << (dev & 63)))) {
       if (cudaFuncSetAttribute(sas_metadata_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)(sizeof(long long) * (kNumArrays * kSmemBatches + 1))) != cudaSuccess)
+                               kSmemCap) != cudaSuccess)
         return SAS_ERR_CUDA;
       attr_done |= 1ull << (dev & 63);
     }

@@ -14,6 +14,8 @@
 //     Rows past a batch's end are evaluated with the same formulas, which is
 //     how the reference behaves when the row cursor overruns the batch.
 //   phase 3: pack faMetadata / fdMetadata (metadata.py:974-1009).
+#include <mutex>
+
 #include "sas_common.cuh"
 
 namespace {
@@ -659,4 +661,67 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   sas_metadata_kernel<<<1, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(A, arrays, core_out, metadata_out,
                                                                                 status);
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of sas_metadata.
+//
+// Some callers cannot call cudaMalloc at the point where they need the
+// schedule: code running while a caching allocator is locked or being
+// torn down, plugins loaded into a host that owns all device memory, and
+// hot loops that must not synchronise (cudaMalloc/cudaFree can). For them
+// the scratch lives in a fixed device array compiled into this library.
+// It is sized for up to kNoAllocMaxBatch requests and kNoAllocMaxCores
+// cores (296,704 bytes), and every GPU that loads the library keeps that
+// array until the process exits.
+namespace {
+constexpr int kNoAllocMaxBatch = 4096;
+constexpr int kNoAllocMaxCores = 64;
+constexpr size_t kNoAllocScratchBytes =
+    ((sizeof(long long) * (kNumArrays * (size_t)kNoAllocMaxBatch + 1) + 255) / 256) * 256 +
+    ((sizeof(int64_t) * 3 * (size_t)kNoAllocMaxCores + 255) / 256) * 256;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+constexpr int kMaxDevices = 64;
+void* g_noalloc_ptr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int sas_metadata_noalloc(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
+                                    const int32_t* cu_seqlens_ori_kv, int32_t n_cu_seqlens_ori_kv,
+                                    const int32_t* seqused_q, int32_t n_seqused_q, const int32_t* seqused_kv,
+                                    int32_t n_seqused_kv, int32_t batch_size, int32_t max_seqlen_q,
+                                    int32_t max_seqlen_kv, int32_t num_heads_q, int32_t num_heads_kv,
+                                    int32_t head_dim, int32_t cmp_topk, int32_t cmp_ratio, int32_t ori_mask_mode,
+                                    int32_t ori_win_left, int32_t layout_q, int32_t layout_kv, int32_t has_cmp_kv,
+                                    int32_t aic_core_num, int32_t* metadata_out, int32_t* status, void* stream) {
+  if (!metadata_out) return SAS_ERR_INVALID_ARG;
+  // the batch size exactly as sas_metadata resolves it (metadata.py:345-350)
+  int64_t B = batch_size;
+  if (n_seqused_q > 0 && seqused_q) B = n_seqused_q;
+  else if (layout_q == SAS_LAYOUT_TND && n_cu_seqlens_q > 0 && cu_seqlens_q) B = n_cu_seqlens_q - 1;
+  if (B > kNoAllocMaxBatch || aic_core_num > kNoAllocMaxCores) return SAS_ERR_NOALLOC_LIMIT;
+  if (!sas::select_device_of(metadata_out)) return SAS_ERR_INVALID_ARG;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SAS_ERR_CUDA;
+  void* scratch = nullptr;
+  {
+    // first call on a device: look up the device address of the array (the
+    // host-side symbol is only a stand-in and must never reach a kernel)
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) {
+        cudaGetLastError();
+        return SAS_ERR_CUDA;
+      }
+      g_noalloc_ptr[dev] = p;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  // every byte of scratch the kernel reads it has written earlier in the same
+  // launch, so nothing needs clearing between calls
+  return sas_metadata(cu_seqlens_q, n_cu_seqlens_q, cu_seqlens_ori_kv, n_cu_seqlens_ori_kv, seqused_q, n_seqused_q,
+                      seqused_kv, n_seqused_kv, batch_size, max_seqlen_q, max_seqlen_kv, num_heads_q, num_heads_kv,
+                      head_dim, cmp_topk, cmp_ratio, ori_mask_mode, ori_win_left, layout_q, layout_kv, has_cmp_kv,
+                      aic_core_num, metadata_out, status, scratch, kNoAllocScratchBytes, stream);
 }

@@ -29,6 +29,7 @@ extern "C" {
 #define SAS_ERR_CUDA 3           /* a CUDA runtime call or launch failed */
 #define SAS_ERR_WORKSPACE 4      /* workspace missing or smaller than required */
 #define SAS_ERR_SCHED_OVERRUN 5  /* device status: scheduler row scan hit its cap */
+#define SAS_ERR_NOALLOC_LIMIT 6  /* request exceeds the fixed scratch of sas_metadata_noalloc */
 #define SAS_ERR_TIMEOUT_BASE 16  /* device status: 16 + id of the bounded wait that ran out */
 
 #define SAS_META_SIZE 1024
@@ -76,6 +77,29 @@ int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
                  int32_t layout_q, int32_t layout_kv, int32_t has_cmp_kv, int32_t aic_core_num,
                  int32_t* metadata_out, int32_t* status,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of sas_metadata. No counterpart in the reference.
+ * For callers that cannot allocate device memory when they need a schedule
+ * (code running inside an allocator or teardown path, plugins whose host owns
+ * all device memory, loops that must not synchronise): the scheduler's
+ * scratch is a fixed device array inside this library (296,704 bytes, held by
+ * every GPU that loads the library until the process exits), so no workspace
+ * is passed and nothing is allocated. Limits: batch <= 4096 requests and
+ * aic_core_num <= 64; larger requests return SAS_ERR_NOALLOC_LIMIT. The first
+ * call on a device looks up the array's device address; make that first call
+ * before any stream capture. All calls share the one array, so calls whose
+ * executions overlap on the GPU (different streams, or different host threads)
+ * race and must be serialised by the caller. Same arguments and output as
+ * sas_metadata otherwise. */
+int sas_metadata_noalloc(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
+                         const int32_t* cu_seqlens_ori_kv, int32_t n_cu_seqlens_ori_kv,
+                         const int32_t* seqused_q, int32_t n_seqused_q,
+                         const int32_t* seqused_kv, int32_t n_seqused_kv,
+                         int32_t batch_size, int32_t max_seqlen_q, int32_t max_seqlen_kv,
+                         int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                         int32_t cmp_topk, int32_t cmp_ratio, int32_t ori_mask_mode, int32_t ori_win_left,
+                         int32_t layout_q, int32_t layout_kv, int32_t has_cmp_kv, int32_t aic_core_num,
+                         int32_t* metadata_out, int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------
  * Forward: the fused sparse shared-KV attention.

@@ -487,10 +487,14 @@ def ours_arm(a, rank, world, local_rank):
         peaks = json.load(open(pk))
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     achieved = work["bytes"] / (attn_ms * 1e-3) / 1e9
+    # DRAM bytes per attention launch from the committed ncu capture of this
+    # workload (profiles/sas_fwd_kernel_<config>_*.md, "traffic_bytes_per_launch")
     traffic = None
-    tf = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tf):
-        traffic = json.load(open(tf)).get(a.config)
+    import glob
+    for pf in glob.glob(os.path.join(ROOT, "profiles", f"sas_fwd_kernel_{a.config.lower()}_*.md")):
+        for ln in open(pf):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                traffic = int(ln.split(":")[1])
     value = tokens_all * a.steps / (total_ms * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,

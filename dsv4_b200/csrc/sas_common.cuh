@@ -203,6 +203,13 @@ __device__ __forceinline__ int named_bar_or(int id, int nthreads, int pred) {
   return (int)r;
 }
 
+// Maximum of v over the 32 lanes of the warp (sm_100a float redux).
+__device__ __forceinline__ float warp_max_f32(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -600,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;   // KV row of the chunk / d within an O^T tile
     const int st = tid - kSoftmaxWarp0 * 32;  // 0..127
     const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    float lsum0 = 0.f, lsum1 = 0.f;     // running sums of heads 2*lane, 2*lane+1 over this warp's rows
+    float lsum0 = 0.f, lsum1 = 0.f;  // running sums of heads 2*lane, 2*lane+1 over this warp's rows
     Walker wk;
     wk.init(p.unit_start, p.T, p.R, r);
     Seg sg;
@@ -629,21 +629,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         sas::tc_fence_after();
         const long long ts0 = tracing ? clock64() : 0;
-        // ---- per-head max over the 128 rows of the chunk
+        // ---- this row's scaled scores (log2 units), one TMEM read per chunk
+        float x[64];
         {
-          float t[64];
           uint32_t ra[32], rb[32];
           sas::tmem_ld32(lane_addr + TM_S, ra);
           sas::tmem_ld32(lane_addr + TM_S + 32, rb);
           sas::tmem_wait_ld();
 #pragma unroll
           for (int h = 0; h < 32; ++h) {
-            t[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
-            t[h + 32] = valid ? __uint_as_float(rb[h]) * p.scale_log2 : -INFINITY;
+            x[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
+            x[h + 32] = valid ? __uint_as_float(rb[h]) * p.scale_log2 : -INFINITY;
           }
-          warp_reduce_scatter64<true>(t, lane);
-          red[quad * 64 + 2 * lane] = t[0];
-          red[quad * 64 + 2 * lane + 1] = t[1];
+        }
+        // ---- per-head max over the warp's 32 rows (redux), then over the 4 warps
+#pragma unroll
+        for (int h = 0; h < 64; h += 4) {
+          float4 w;
+          w.x = sas::warp_max_f32(x[h]);
+          w.y = sas::warp_max_f32(x[h + 1]);
+          w.z = sas::warp_max_f32(x[h + 2]);
+          w.w = sas::warp_max_f32(x[h + 3]);
+          if (lane == 0) *reinterpret_cast<float4*>(red + quad * 64 + h) = w;
         }
         sas::named_bar_sync(1, 128);
         int need = 0;
@@ -676,29 +683,22 @@ __global__ void __launch_bounds__(kThreads, 1)
             sas::tmem_wait_st();
           }
         }
-        // ---- p = 2^(x - m); P^T to smem (128 B rows, 128B swizzle); row sums
+        // ---- p = 2^(x - m) (masked rows give 0); P^T to smem (128 B rows,
+        // 128B swizzle) rounded to the I/O dtype; l sums the unrounded p
         {
-          float pv[64];
-          uint32_t ra[32], rb[32];
-          sas::tmem_ld32(lane_addr + TM_S, ra);
-          sas::tmem_ld32(lane_addr + TM_S + 32, rb);
-          sas::tmem_wait_ld();
 #pragma unroll
-          for (int h = 0; h < 32; ++h) {
-            pv[h] = valid ? sas::ex2(__uint_as_float(ra[h]) * p.scale_log2 - m_run[h]) : 0.f;
-            pv[h + 32] = valid ? sas::ex2(__uint_as_float(rb[h]) * p.scale_log2 - m_run[h + 32]) : 0.f;
-          }
+          for (int h = 0; h < 64; ++h) x[h] = sas::ex2(x[h] - m_run[h]);
           uint8_t* prow = pbuf + row * 128;
 #pragma unroll
           for (int c16 = 0; c16 < 8; ++c16) {
             const int h = c16 * 8;
             *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
-                make_uint4(IO::pack(pv[h], pv[h + 1]), IO::pack(pv[h + 2], pv[h + 3]),
-                           IO::pack(pv[h + 4], pv[h + 5]), IO::pack(pv[h + 6], pv[h + 7]));
+                make_uint4(IO::pack(x[h], x[h + 1]), IO::pack(x[h + 2], x[h + 3]),
+                           IO::pack(x[h + 4], x[h + 5]), IO::pack(x[h + 6], x[h + 7]));
           }
-          warp_reduce_scatter64<false>(pv, lane);
-          lsum0 += pv[0];
-          lsum1 += pv[1];
+          warp_reduce_scatter64<false>(x, lane);
+          lsum0 += x[0];
+          lsum1 += x[1];
         }
         sas::fence_proxy_async_smem();
         sas::tc_fence_before();

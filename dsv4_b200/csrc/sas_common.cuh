@@ -82,6 +82,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ------------------------------------------------------------------- TMA
+// Programmatic dependent launch: a kernel launched with the programmatic
+// stream-serialization attribute may start before the previous kernel on the
+// stream ends; pdl_wait() blocks until that kernel has completed and its
+// memory is visible (a no-op without the attribute). pdl_launch_dependents()
+// lets the next such kernel start launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Prefetch the 128-byte line holding `addr` into L2.
+__device__ __forceinline__ void prefetch_l2_line(const void* addr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(addr)));
+}
 __device__ __forceinline__ void tma_prefetch_desc(const void* desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(desc)) : "memory");
 }

@@ -1,6 +1,6 @@
 // Fused sparse shared-KV attention forward for B200 (sm_100a).
 //
-// Three kernels, all launched by sas_sparse_attn_sharedkv_fwd on the caller's
+// Two kernels, both launched by sas_sparse_attn_sharedkv_fwd on the caller's
 // stream:
 //
 // 1. sas_plan_kernel (1 CTA): walks the metadata's per-core windows of
@@ -10,40 +10,41 @@
 //    its work in 128-row chunks: ceil((win_left+1)/128) window chunks plus
 //    ceil(n_cmp/128) compressed chunks, n_cmp = min(K, threshold) for SCFA,
 //    threshold for CFA (threshold = (s_g+1)//ratio, golden.py:41-51).
-//    An exclusive scan gives each token's first chunk-unit.
+//    An exclusive scan gives each token's first chunk-unit. Output rows of
+//    tokens without work are zeroed (golden.py leaves them zero), and the
+//    split-token arrival counters are cleared.
 //
 // 2. sas_fwd_kernel (persistent, R x G CTAs, one per SM): the unit sequence
 //    is cut into R equal contiguous ranges; the G CTAs of a range each own
 //    64 query heads (head group g) and walk the same rows, so the second
 //    reader of every KV row hits L2. Per CTA, warp-specialised:
-//      warp 0   producer: resolves window positions / top-k ids through the
-//               block tables (kernel.py:285-401, 686-766), publishes a
-//               128-bit row-validity mask and gathers the 128 rows x 512
-//               cols chunk with TMA tile::gather4 in eight 64-col slabs
-//               (128B swizzle); masked rows use an out-of-range row, so TMA
-//               zero-fills them without touching HBM.
-//      warp 1   MMA issuer (one thread): transposed attention so the KV rows
-//               fill the M=128 datapath and the 64 heads are N:
+//      warps 0-3 loaders: one KV row per thread; resolve window positions /
+//               top-k ids through the block tables (kernel.py:285-401,
+//               686-766), publish a 128-bit row-validity mask, and gather the
+//               128 rows x 512 cols chunk with 16-byte cp.async into eight
+//               64-col slabs in the 128B-swizzled K-major layout (masked rows
+//               are zero-filled without a read).
+//      warp 8   MMA issuer (one thread) and TMEM owner: transposed attention
+//               so the KV rows fill the M=128 datapath and the 64 heads are N:
 //                 S^T[128 x 64]  = K[128 x 512] . Q^T          (K-major A and B)
 //                 O^T[512 x 64] += V^T[512 x 128] . P^T[128 x 64] (4 MMAs of
 //               M=128; V^T is the SAME smem tile read MN-major, since K=V)
 //               TMEM: S^T in cols [0,64), O^T tiles in cols [64,320).
-//      warps 2-5 softmax / epilogue: one thread per KV row (TMEM lane). The
+//      warps 4-7 softmax / epilogue: one thread per KV row (TMEM lane). The
 //               row mask (window idx <= s_g; compressed 0 <= idx < threshold,
-//               scan stopped at the first -1) sets scores to -inf; the
-//               per-head running max is a warp reduce-scatter plus a 4-way
-//               smem merge; the state starts at (m, l) = (sink, 1) in log2
-//               units (kernel.py:594-618, golden.py:156-160) and O^T is only
-//               rescaled when a head's max grows by more than 2^8. P is
-//               rounded to the I/O dtype before P.V while l sums the
-//               unrounded p (golden.py:191-195). Epilogue: O/l, lse = m+ln l.
-//    A token whose chunks all fall in one range is finished in place
-//    (sink folded in); a token cut by a range boundary leaves normalised
-//    partials (o, lse2) in the workspace.
-//
-// 3. sas_combine_kernel: for every cut token, lse = log2(sum 2^lse_i +
-//    2^sink), out = sum 2^(lse_i - lse) o_i; also zero-fills output rows of
-//    tokens that have no work (BSND padding), as golden.py leaves them zero.
+//               scan stopped at the first -1) sets scores to -inf; per-head
+//               maxima are warp redux.max plus a 4-way smem merge; the state
+//               starts at (m, l) = (sink, 1) in log2 units (kernel.py:594-618,
+//               golden.py:156-160) and O^T is only rescaled when a head's max
+//               grows by more than 2^8. P is rounded to the I/O dtype before
+//               P.V while l sums the unrounded p (golden.py:191-195).
+//               Epilogue: O/l, lse = m + ln l.
+//    A token whose chunks all fall in one range is finished in place (sink
+//    folded in). A token cut by range boundaries leaves normalised partials
+//    (o, lse2) in the workspace; the CTA that lands the token's last partial
+//    merges them: lse = log2(sum 2^lse_i + 2^sink), out = sum 2^(lse_i-lse) o_i.
+//    Every wait is bounded (%globaltimer); a wait that runs out sets the
+//    status word and the CTA stands down.
 #include <cuda.h>
 #include <cstdio>
 #include <mutex>
@@ -62,7 +63,9 @@ constexpr int kLoaderWarps = 4;         // warps 0-3: cp.async loaders
 constexpr int kLoaderThreads = 32 * kLoaderWarps;
 constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax / epilogue
 constexpr int kMmaWarp = 8;             // warp 8: TMEM owner and MMA issuer
-constexpr int kThreads = 32 * 9;
+constexpr int kCoordWarp = 9;           // warp 9: row resolution + L2 prefetch, runs ahead
+constexpr int kThreads = 32 * 10;
+constexpr int CD = 4;                    // depth of the row-coordinate ring (chunks)
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -75,13 +78,16 @@ constexpr int OFF_MISC = OFF_P + CH * 128;               // +16 KB
 constexpr int M_BAR = 0;         // 32 mbarriers x 8 B
 constexpr int M_TMEM = 256;      // tmem base address
 constexpr int M_ABORT = 260;
-constexpr int M_MASK = 272;      // 2 x 4 words
-constexpr int M_FIRST = 320;     // 2 x 4 ints
+constexpr int M_CMASK = 272;     // CD x 4 words: row-validity mask per ring slot
+constexpr int M_LWORD = 384;     // 3 words: group B (loader warps) OR
+constexpr int M_SWORD = 400;     // 3 words: group A (softmax warps) OR
+constexpr int M_RANGE = 416;     // RangeInfo of this CTA (4 ints)
 constexpr int M_RED = 512;       // 4 x 64 floats = 1 KB
 constexpr int M_MRUN = 1536;     // 64 floats
 constexpr int M_ALPHA = 1792;    // 64 floats
 constexpr int M_INV = 2048;      // 64 floats
-constexpr int MISC_BYTES = 2304;
+constexpr int M_COORD = 2304;    // CD x 128 int32: pool row per chunk row (-1 = masked)
+constexpr int MISC_BYTES = M_COORD + CD * CH * 4;
 constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES + 1024;  // + alignment slack
 
 // barrier indices
@@ -93,8 +99,10 @@ constexpr int B_SFULL = 18;
 constexpr int B_PREADY = 19;
 constexpr int B_OFULL = 20;
 constexpr int B_OEMPTY = 21;
-constexpr int B_MFULL = 22;      // 2
-constexpr int B_MEMPTY = 24;     // 2
+constexpr int B_CFULL = 22;      // CD: coordinate ring slot written
+constexpr int B_LSYNC = 26;      // group barrier of softmax group B (warps 0-3)
+constexpr int B_SSYNC = 27;      // group barrier of softmax group A (warps 4-7)
+constexpr int B_CEMPTY = 28;     // CD: slot read by the 4 loader and 4 softmax warps
 
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TM_S = 0;
@@ -114,6 +122,8 @@ struct PlanParams {
   int H, dtype_bytes;
   void* out;            // rows of tokens without work are zeroed here
   float* lse;
+  int32_t* merge_cnt;   // [n_cnt] split-token arrival counters, zeroed here
+  int n_cnt;
 };
 
 struct FwdParams {
@@ -133,6 +143,7 @@ struct FwdParams {
   const int32_t* unit_start;
   float* part_o;    // [R*2*G][64][512]
   float* part_lse;  // [R*2*G][64]
+  int32_t* merge_cnt;  // [R*G*2]: arrivals per cut token, keyed by (first range, group, head half)
   int32_t* status;
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
@@ -143,7 +154,8 @@ struct FwdParams {
 enum TraceSlot {
   TR_TOTAL = 0, TR_P_COORD, TR_P_WAIT_EMPTY, TR_P_WAIT_MASK, TR_P_ISSUE, TR_M_WAIT_Q, TR_M_WAIT_FULL,
   TR_M_WAIT_P, TR_M_WAIT_O, TR_S_WAIT_MASK, TR_S_WAIT_S, TR_S_SOFTMAX, TR_S_WAIT_O, TR_S_EPI, TR_CHUNKS,
-  TR_SEGS, TR_E_TMEM, TR_E_STAGE, TR_E_COPY, TR_E_RED, TR_NSLOTS = 20
+  TR_SEGS, TR_E_TMEM, TR_E_STAGE, TR_E_COPY, TR_E_RED, TR_S_LD, TR_S_SYNC1, TR_S_SYNC2, TR_S_EXP,
+  TR_S_SUM, TR_S_FENCE, TR_S_RESCALE, TR_S_MAX, TR_NSLOTS = 28
 };
 
 __device__ __forceinline__ int py_floordiv(int a, int b) {
@@ -154,6 +166,8 @@ __device__ __forceinline__ int py_floordiv(int a, int b) {
 
 // ------------------------------------------------------------------ plan
 __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
+  sas::pdl_launch_dependents();  // the attention kernel's prologue may start now
+  sas::pdl_wait();               // the metadata may come from the kernel before
   __shared__ int s_smax;
   __shared__ int s_lin[SAS_AIC_CORE_NUM][2];
   __shared__ int s_en[SAS_AIC_CORE_NUM];
@@ -178,6 +192,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
   }
   __syncthreads();
   const int smax = s_smax;
+  for (int i = tid; i < p.n_cnt; i += blockDim.x) p.merge_cnt[i] = 0;
   if (tid < SAS_AIC_CORE_NUM) {
     const int32_t* row = p.meta + tid * 8;
     s_en[tid] = row[0];
@@ -263,23 +278,70 @@ struct Seg {
   bool complete;
 };
 
-struct Walker {
-  int pos, end, t, u0;
-  const int32_t* us;
-  __device__ void init(const int32_t* unit_start, int T, int R, int r) {
-    us = unit_start;
-    const int U = us[T];
-    const int u = (U + R - 1) / R;
-    u0 = min(r * u, U);
-    pos = u0;
-    end = min(u0 + u, U);
-    // largest t with unit_start[t] <= u0
-    int lo = 0, hi = T - 1;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (us[mid] <= u0) lo = mid; else hi = mid - 1;
+// Largest t in [0, T) with us[t] <= x (us non-decreasing, us[0] <= x),
+// found by one warp in 32-way steps: ceil(log32 T) rounds of loads instead of
+// log2 T dependent ones. Every lane returns the result.
+__device__ __forceinline__ int warp_last_le(const int32_t* us, int T, int x, int lane) {
+  int lo = 0, hi = T - 1;
+  while (hi > lo) {
+    const int step = (hi - lo + 32) / 32;  // probes lo + k*step, k = 1..32, cover (lo, hi]
+    const int probe = lo + (lane + 1) * step;
+    const bool le = probe <= hi && us[probe] <= x;
+    const unsigned b = __ballot_sync(0xffffffffu, le);
+    if (b == 0) {
+      hi = lo + step - 1;
+    } else {
+      const int k = 31 - __clz(b);  // last probe with us[probe] <= x
+      lo = lo + (k + 1) * step;
+      hi = min(hi, lo + step - 1);
     }
-    t = lo;
+  }
+  return lo;
+}
+
+// Chunks a token may hold beyond a range's length before it is cut across
+// ranges: a cut costs the partial write-back and the merge, about this many
+// chunks of work.
+constexpr int kCutCost = 3;
+
+// First unit of range r: r*u, moved back to the start of the token holding
+// it unless that token is too long to keep whole (more than u + kCutCost
+// units). Boundaries inside a cut token are therefore always r*u exactly.
+__device__ __forceinline__ int range_start(const int32_t* us, int T, int U, int u, int r, int lane) {
+  if (r <= 0) return 0;
+  const long long x = (long long)r * u;
+  if (x >= U) return U;
+  const int t = warp_last_le(us, T, (int)x, lane);
+  const int st = us[t], n = us[t + 1] - st;
+  return (x == st || n > u + kCutCost) ? (int)x : st;
+}
+
+// A CTA's unit range [u0, end) and the token holding u0, computed once per
+// CTA by one warp and shared through shared memory.
+struct RangeInfo {
+  int u0, end, t, u;
+};
+
+__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, int T, int R, int r, int lane) {
+  RangeInfo ri;
+  const int U = us[T];
+  ri.u = (U + R - 1) / R;
+  ri.u0 = range_start(us, T, U, ri.u, r, lane);
+  ri.end = r + 1 >= R ? U : range_start(us, T, U, ri.u, r + 1, lane);
+  ri.t = ri.u0 < U ? warp_last_le(us, T, ri.u0, lane) : T - 1;
+  return ri;
+}
+
+struct Walker {
+  int pos, end, t, u0, u;
+  const int32_t* us;
+  __device__ void init(const int32_t* unit_start, const RangeInfo& ri) {
+    us = unit_start;
+    u = ri.u;
+    u0 = ri.u0;
+    pos = u0;
+    end = ri.end;
+    t = ri.t;
   }
   __device__ bool next(Seg& s) {
     if (pos >= end) return false;
@@ -326,11 +388,14 @@ struct IoType<1> {
 
 // Reduce 64 per-thread values across the 32 lanes of a warp; afterwards
 // v[0], v[1] hold the reduction for columns 2*lane and 2*lane+1.
-template <bool IS_MAX>
-__device__ __forceinline__ void warp_reduce_scatter64(float (&v)[64], int lane) {
+// Warp reduce-scatter of N = 32 or 64 per-lane columns: afterwards lane l
+// holds the reduction over the 32 lanes for columns [l*N/32, (l+1)*N/32) in
+// v[0 .. N/32). Five exchange rounds, each halving the live columns.
+template <int N, bool IS_MAX>
+__device__ __forceinline__ void warp_reduce_scatter(float (&v)[N], int lane) {
 #pragma unroll
   for (int step = 0; step < 5; ++step) {
-    const int half = 32 >> step;
+    const int half = (N / 2) >> step;
     const int m = 16 >> step;
     const bool up = (lane & m) != 0;
 #pragma unroll
@@ -352,6 +417,38 @@ __device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, volatile i
   return r;
 }
 
+// Barrier among the 4 warps of one role, with a bounded wait (a named
+// barrier cannot time out, and a sibling warp that left on an abort would
+// strand the others in it). Lane 0 of every warp arrives on `bar` (count 4);
+// `pred` is OR-reduced into words[ph % 3]; warp `lead` clears the word the
+// sync after next uses before it arrives: every warp has read that word
+// (two syncs back) before it arrived at the previous sync. Returns false
+// when the wait gave up.
+struct GroupSync {
+  uint64_t* bar;
+  uint32_t* words;
+  uint32_t ph;
+  __device__ __forceinline__ bool sync_or(int pred, int lane, bool lead, int& result, volatile int* abort_flag,
+                                          int* status, int where) {
+    const bool any = __any_sync(0xffffffffu, pred);
+    __syncwarp();
+    const uint32_t k = ph % 3;
+    if (lane == 0) {
+      if (any) atomicOr(&words[k], 1u);
+      if (lead) words[(k + 1) % 3] = 0;
+      sas::mbar_arrive(bar);
+    }
+    const bool ok = sas::mbar_wait(bar, ph & 1, abort_flag, status, where);
+    result = ok ? (int)*reinterpret_cast<volatile uint32_t*>(&words[k]) : 0;
+    ++ph;
+    return ok;
+  }
+  __device__ __forceinline__ bool sync(int lane, bool lead, volatile int* abort_flag, int* status, int where) {
+    int unused;
+    return sync_or(0, lane, lead, unused, abort_flag, status, where);
+  }
+};
+
 // 16-byte async copy global -> shared; src_bytes = 0 writes zeros without reading.
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
@@ -361,7 +458,323 @@ __device__ __forceinline__ void cp_async_arrive(uint64_t* bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(sas::smem_u32(bar)) : "memory");
 }
 
+// One softmax group: 4 warps that cover TMEM lanes 0-127 (one KV row of the
+// chunk per thread) and 32 of the CTA's 64 heads, S^T / O^T columns
+// [hb, hb+32). Group A is warps 4-7 (hb = 0); group B is the loader warps
+// 0-3 (hb = 32), which are otherwise idle while the chunk they copied is in
+// softmax. The groups own disjoint heads, so they never wait on each other.
+struct SmGroup {
+  int hb, half;         // first head column (0 or 32), hb / 32
+  int quad, lane, gst;  // TMEM lane quadrant, lane, row = quad*32 + lane
+  bool lead;
+  GroupSync gs;
+  float lsum;           // running sum of head hb+lane over this warp's 32 rows
+  uint32_t lane_addr;   // TMEM address of this warp's lane quadrant
+  uint32_t seg;         // segments finished
+};
+
+// Shared-memory scratch of the softmax groups (disjoint columns per group).
+struct SmShared {
+  float* red;     // [4 quads][64 heads]
+  float* m_run;   // [64] running max, log2 units
+  float* alpha;   // [64] rescale factors / merge scratch
+  float* inv;     // [64] 1 / l
+  uint8_t* pbuf;  // P^T: 128 rows x 64 heads, 128B-swizzled
+};
+
+// Split-KV merge of one cut token for the heads [hb, hb+32) of group g, run
+// by one softmax group of the CTA that wrote the token's last partial:
+// lse = log2(sum_i 2^lse_i + 2^sink), out = sum_i 2^(lse_i - lse) o_i.
+// Phase 1: thread c folds head hb+c's partial LSEs in one online pass.
+// Phase 2: every thread owns one float4 column and accumulates 8 heads at a
+// time, so 8 independent loads are in flight per partial. Partials come
+// from other CTAs, so they are read through L2 (.cg).
+__device__ __forceinline__ size_t part_slot(const FwdParams& p, int rr, int r0, int ust, int u, int g) {
+  return ((size_t)rr * 2 + ((rr == r0 && rr * u < ust) ? 1 : 0)) * p.G + g;
+}
+
 template <int DT>
+__device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g, int r0, int r1, int ust, int u,
+                                                SmGroup& G, float* lse_s, volatile int* abort_flag) {
+  using IO = IoType<DT>;
+  const int ns = r1 - r0 + 1;
+  const int hn = min(HG, p.H - g * HG);  // heads of this group
+  const int hend = min(G.hb + 32, hn);
+  if (G.hb + G.gst < hend && G.gst < 32) {
+    const int c = G.hb + G.gst, h = g * HG + c;
+    float m = p.sinks[h] * kLog2e, den = 1.f;
+    for (int i = 0; i < ns; ++i) {
+      const float l = __ldcg(p.part_lse + part_slot(p, r0 + i, r0, ust, u, g) * HG + c);
+      const float mn = fmaxf(m, l);
+      den = den * sas::ex2(m - mn) + sas::ex2(l - mn);
+      m = mn;
+    }
+    const float L = m + __log2f(den);
+    lse_s[c] = L;
+    if (p.lse) p.lse[(size_t)t * p.H + h] = L * kLn2;
+  }
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 22)) return false;
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + ((size_t)t * p.H + g * HG) * D;
+  constexpr int kHB = 8;
+#pragma unroll 1
+  for (int h0 = G.hb; h0 < hend; h0 += kHB) {
+    float4 acc[kHB];
+#pragma unroll
+    for (int j = 0; j < kHB; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int i = 0; i < ns; ++i) {
+      const size_t slot = part_slot(p, r0 + i, r0, ust, u, g);
+      const float* pl = p.part_lse + slot * HG + h0;
+      const float4* po = reinterpret_cast<const float4*>(p.part_o + (slot * HG + h0) * D) + G.gst;
+      float4 v[kHB];
+      float w[kHB];
+#pragma unroll
+      for (int j = 0; j < kHB; ++j) {
+        v[j] = __ldcg(po + j * (D / 4));
+        w[j] = __ldcg(pl + j);
+      }
+#pragma unroll
+      for (int j = 0; j < kHB; ++j) {
+        const float wj = sas::ex2(w[j] - lse_s[h0 + j]);
+        acc[j].x += wj * v[j].x;
+        acc[j].y += wj * v[j].y;
+        acc[j].z += wj * v[j].z;
+        acc[j].w += wj * v[j].w;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kHB; ++j) {
+      if (h0 + j < hend) {
+        uint2 o;
+        o.x = IO::pack(acc[j].x, acc[j].y);
+        o.y = IO::pack(acc[j].z, acc[j].w);
+        reinterpret_cast<uint2*>(outp + (size_t)(h0 + j) * D)[G.gst] = o;
+      }
+    }
+  }
+  return true;
+}
+
+// Softmax of one chunk for the group's 32 heads: scores from S^T, per-head
+// max over the chunk's 128 rows (warp redux + 4-way smem merge), lazy O^T
+// rescale when a running max grows by more than tau, p = 2^(x - m) written to
+// P^T rounded to the I/O dtype, l += sum of the unrounded p.
+template <int DT>
+__device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
+                                              uint32_t gchunk, bool first, bool valid, int g,
+                                              volatile int* abort_flag, bool tracing, unsigned long long* tr) {
+  using IO = IoType<DT>;
+  if (first) {
+    if (G.gst < 32) {
+      const int h = g * HG + G.hb + G.gst;
+      S.m_run[G.hb + G.gst] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
+    }
+    G.lsum = 0.f;
+  }
+  if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
+  sas::tc_fence_after();
+  const long long ts0 = tracing ? clock64() : 0;
+  float x[32];
+  {
+    uint32_t ra[32];
+    sas::tmem_ld32(G.lane_addr + TM_S + G.hb, ra);
+    sas::tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < 32; ++h) x[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
+  }
+  long long tq = tracing ? clock64() : 0;
+  if (tracing) tr[TR_S_LD] += tq - ts0;
+#pragma unroll
+  for (int h = 0; h < 32; h += 4) {
+    float4 w;
+    w.x = sas::warp_max_f32(x[h]);
+    w.y = sas::warp_max_f32(x[h + 1]);
+    w.z = sas::warp_max_f32(x[h + 2]);
+    w.w = sas::warp_max_f32(x[h + 3]);
+    if (G.lane == 0) *reinterpret_cast<float4*>(S.red + G.quad * 64 + G.hb + h) = w;
+  }
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_MAX] += t2 - tq;
+    tq = t2;
+  }
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 16)) return false;
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_SYNC1] += t2 - tq;
+    tq = t2;
+  }
+  int need = 0;
+  if (G.gst < 32) {
+    const int c = G.hb + G.gst;
+    const float mx = fmaxf(fmaxf(S.red[c], S.red[64 + c]), fmaxf(S.red[128 + c], S.red[192 + c]));
+    const float mo = S.m_run[c];
+    float al = 1.f;
+    if (mx > mo + p.tau) {
+      al = sas::ex2(mo - mx);
+      S.m_run[c] = mx;
+      need = 1;
+    }
+    S.alpha[c] = al;
+  }
+  if (!G.gs.sync_or(need, G.lane, G.lead, need, abort_flag, p.status, 17)) return false;
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_SYNC2] += t2 - tq;
+    tq = t2;
+  }
+  if (need) {
+    G.lsum *= S.alpha[G.hb + G.lane];
+    if (!first) {
+      // O^T holds chunks up to i-1: S^T(i) completing implies P.V(i-1) has
+#pragma unroll 1
+      for (int j = 0; j < 4; ++j) {
+        uint32_t o[32];
+        sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+        sas::tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 32; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * S.alpha[G.hb + h]);
+        sas::tmem_st32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+      }
+      sas::tmem_wait_st();
+    }
+  }
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_RESCALE] += t2 - tq;
+    tq = t2;
+  }
+#pragma unroll
+  for (int h = 0; h < 32; ++h) x[h] = sas::ex2(x[h] - S.m_run[G.hb + h]);
+  uint8_t* prow = S.pbuf + G.gst * 128;
+#pragma unroll
+  for (int c4 = 0; c4 < 4; ++c4) {
+    const int cc = (G.hb >> 3) + c4;  // 16-byte column chunk of the 128-byte row
+    const int h = c4 * 8;
+    *reinterpret_cast<uint4*>(prow + ((cc ^ (G.gst & 7)) << 4)) =
+        make_uint4(IO::pack(x[h], x[h + 1]), IO::pack(x[h + 2], x[h + 3]), IO::pack(x[h + 4], x[h + 5]),
+                   IO::pack(x[h + 6], x[h + 7]));
+  }
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_EXP] += t2 - tq;
+    tq = t2;
+  }
+  warp_reduce_scatter<32, false>(x, G.lane);
+  G.lsum += x[0];
+  if (tracing) {
+    const long long t2 = clock64();
+    tr[TR_S_SUM] += t2 - tq;
+    tq = t2;
+  }
+  sas::fence_proxy_async_smem();
+  sas::tc_fence_before();
+  sas::mbar_arrive(&bars[B_PREADY]);
+  if (tracing) tr[TR_S_FENCE] += clock64() - tq;
+  if (tracing) {
+    tr[TR_S_SOFTMAX] += clock64() - ts0;
+    tr[TR_CHUNKS] += 1;
+  }
+  return true;
+}
+
+// Epilogue of one segment for the group's heads: l over the 4 quads, then
+// out = O/l with the sink folded into l (complete token) or a normalised
+// partial (o, lse2) for a token cut across ranges; the group that lands a cut
+// token's last partial merges all of them.
+template <int DT>
+__device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
+                                                 const Seg& sg, int r, int g, int u, volatile int* abort_flag,
+                                                 bool tracing, unsigned long long* tr) {
+  using IO = IoType<DT>;
+  if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
+  sas::tc_fence_after();
+  const long long te0 = tracing ? clock64() : 0;
+  S.red[G.quad * 64 + G.hb + G.lane] = G.lsum;
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 18)) return false;
+  const size_t pslot = ((size_t)r * 2 + sg.which) * p.G + g;
+  if (G.gst < 32) {
+    const int c = G.hb + G.gst, h = g * HG + c;
+    const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
+    const float m = S.m_run[c];
+    if (sg.complete) {
+      const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
+      const float Lf = L + sas::ex2(sink - m);
+      S.inv[c] = 1.f / Lf;
+      if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+    } else {
+      S.inv[c] = L > 0.f ? 1.f / L : 0.f;
+      p.part_lse[pslot * HG + c] = L > 0.f ? m + __log2f(L) : -INFINITY;
+    }
+  }
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 19)) return false;
+  if (tracing) tr[TR_E_RED] += clock64() - te0;
+  const int row = G.gst;  // d within an O^T tile
+  if (sg.complete) {
+    // direct stores: lanes pair up (row, row^1); the even lane stores head h
+    // for both rows, the odd lane head h+16 (4-byte stores; no shared-memory
+    // staging, which would compete with the MMA operand reads)
+    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
+    const bool odd = G.lane & 1;
+    const int d_even = row & ~1;
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint32_t o[32];
+      sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+      sas::tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float v0 = __uint_as_float(o[h]) * S.inv[G.hb + h];
+        const float v1 = __uint_as_float(o[h + 16]) * S.inv[G.hb + h + 16];
+        const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+        const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
+        const int hh = g * HG + G.hb + (odd ? h + 16 : h);
+        if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+      }
+    }
+  } else {
+    float* po = p.part_o + pslot * HG * D;
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint32_t o[32];
+      sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+      sas::tmem_wait_ld();
+#pragma unroll
+      for (int h = 0; h < 32; ++h) po[(size_t)(G.hb + h) * D + j * 128 + row] = __uint_as_float(o[h]) * S.inv[G.hb + h];
+    }
+  }
+  sas::tc_fence_before();
+  sas::mbar_arrive(&bars[B_OEMPTY]);
+  ++G.seg;
+  if (!sg.complete) {
+    // ---- fused split-KV merge: every range covering the token adds one
+    // arrival (per head half) to the counter of the token's first range
+    __threadfence();
+    if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 20)) return false;
+    const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
+    const int r0 = ust / u, r1 = (ust + un - 1) / u;
+    int mine = 0, is_last = 0;
+    if (G.gst == 0) {
+      int32_t* cnt = p.merge_cnt + ((size_t)r0 * p.G + g) * 2 + G.half;
+      mine = atomicAdd(cnt, 1) == r1 - r0;
+      if (mine) *cnt = 0;  // every arrival is in: reset for the next launch
+    }
+    if (!G.gs.sync_or(mine, G.lane, G.lead, is_last, abort_flag, p.status, 21)) return false;
+    if (is_last) {
+      __threadfence();
+      if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, ust, u, G, S.alpha, abort_flag)) return false;
+    }
+  }
+  if (tracing) {
+    tr[TR_S_EPI] += clock64() - te0;
+    tr[TR_SEGS] += 1;
+  }
+  return true;
+}
+
+// TRACE = true builds the diagnostics variant that accumulates per-role cycle
+// counters into p.trace; the production variant carries none of that state.
+template <int DT, bool TRACE>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -371,12 +784,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + M_BAR);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + M_ABORT);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + M_TMEM);
-  uint32_t* mask_words = reinterpret_cast<uint32_t*>(misc + M_MASK);    // [2][4]
-  int* first_neg = reinterpret_cast<int*>(misc + M_FIRST);               // [2][4]
+  uint32_t* cmask = reinterpret_cast<uint32_t*>(misc + M_CMASK);        // [CD][4]
+  int32_t* coords = reinterpret_cast<int32_t*>(misc + M_COORD);          // [CD][128]
   float* red = reinterpret_cast<float*>(misc + M_RED);
   float* m_run = reinterpret_cast<float*>(misc + M_MRUN);
   float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
+  const SmShared sm{red, m_run, alpha_s, inv_s, smem + OFF_P};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
@@ -389,12 +803,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas::mbar_init(&bars[B_QFULL], 1);
     sas::mbar_init(&bars[B_QEMPTY], 1);
     sas::mbar_init(&bars[B_SFULL], 1);
-    sas::mbar_init(&bars[B_PREADY], 128);
+    sas::mbar_init(&bars[B_PREADY], 256);
     sas::mbar_init(&bars[B_OFULL], 1);
-    sas::mbar_init(&bars[B_OEMPTY], 128);
-    for (int i = 0; i < 2; ++i) {
-      sas::mbar_init(&bars[B_MFULL + i], kLoaderThreads / 32);
-      sas::mbar_init(&bars[B_MEMPTY + i], 128);
+    sas::mbar_init(&bars[B_OEMPTY], 256);
+    for (int i = 0; i < CD; ++i) {
+      sas::mbar_init(&bars[B_CFULL + i], 1);
+      sas::mbar_init(&bars[B_CEMPTY + i], 8);
+    }
+    sas::mbar_init(&bars[B_SSYNC], 4);
+    sas::mbar_init(&bars[B_LSYNC], 4);
+    for (int i = 0; i < 3; ++i) {
+      reinterpret_cast<uint32_t*>(misc + M_SWORD)[i] = 0;
+      reinterpret_cast<uint32_t*>(misc + M_LWORD)[i] = 0;
     }
     *abort_flag = 0;
     sas::fence_mbar_init();
@@ -409,31 +829,139 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas::tmem_alloc(tmem_slot, TMEM_COLS);
     sas::tmem_relinquish();
   }
-  if (tid == 0) sas::tma_prefetch_desc(&tm_q);
+  // everything above overlaps the plan kernel; its outputs are read below
+  sas::pdl_wait();
+  if (warp == 0) {
+    const RangeInfo ri = compute_range(p.unit_start, p.T, p.R, r, lane);
+    if (lane == 0) *reinterpret_cast<RangeInfo*>(misc + M_RANGE) = ri;
+  }
+  if (tid == 32) sas::tma_prefetch_desc(&tm_q);
   sas::tc_fence_before();
   __syncthreads();
   sas::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const bool tracing = p.trace != nullptr;
+  constexpr bool tracing = TRACE;
   unsigned long long tr[TR_NSLOTS];
 #pragma unroll
   for (int i = 0; i < TR_NSLOTS; ++i) tr[i] = 0;
   const long long t_start = tracing ? clock64() : 0;
 
-  if (warp < kLoaderWarps) {
-    // =============================== loaders: one KV row per thread per chunk
+  if (warp == kCoordWarp) {
+    // =============================== row resolution, up to CD chunks ahead
+    // Lane l resolves rows l, l+32, l+64, l+96 of every chunk through the
+    // block tables (kernel.py:285-401, 686-766), writes the pool row (or -1)
+    // and the validity mask into the ring, and starts each valid row on its
+    // way into L2, so the loaders' copies later hit L2.
+    Walker wk;
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    Seg sg;
+    uint32_t gchunk = 0;
+    bool ok = true;
+    while (ok && wk.next(sg)) {
+      const TokInfo ti = p.tok[sg.t];
+      // the compressed scan stops at the first -1 (golden.py:55-56): a range
+      // that starts inside a token looks for one in the slots before it
+      bool stopped = false;
+      const int cmp_c0 = max(sg.cb - p.n_win_chunks, 0);
+      if (p.scenario == 3 && cmp_c0 > 0) {
+        const int lim = min(cmp_c0 * CH, ti.n_cmp);
+        const int32_t* ip = p.idx + (size_t)sg.t * p.K;
+        int neg = 0;
+        for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
+        stopped = __any_sync(0xffffffffu, neg);
+      }
+      for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
+        const long long tc0 = tracing ? clock64() : 0;
+        const bool is_win = c < p.n_win_chunks;
+        const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
+        int coord[4];
+        bool val[4];
+        if (is_win) {
+          const int lo = max(ti.s_g - p.win_left, 0);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int pos = lo + c * CH + k * 32 + lane;
+            val[k] = (ti.s_g >= 0) && pos <= ti.s_g;
+            const int blk = val[k] ? p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs] : -1;
+            val[k] = val[k] && blk >= 0;
+            coord[k] = blk * p.ori_bs + pos % p.ori_bs;
+          }
+        } else {
+          int id[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = (c - p.n_win_chunks) * CH + k * 32 + lane;
+            val[k] = e < ti.n_cmp;
+            id[k] = e;
+            if (p.scenario == 3) id[k] = val[k] ? p.idx[(size_t)sg.t * p.K + e] : 0;
+          }
+          if (p.scenario == 3) {
+            int cf = CH;  // first -1 of this chunk, in row order
+#pragma unroll
+            for (int k = 3; k >= 0; --k) {
+              const unsigned bal = __ballot_sync(0xffffffffu, val[k] && id[k] == -1);
+              if (bal) cf = k * 32 + __ffs(bal) - 1;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              val[k] = val[k] && !stopped && k * 32 + lane < cf && id[k] >= 0 && id[k] < ti.thr;
+            stopped = stopped || cf < CH;
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) val[k] = val[k] && id[k] < ti.thr;
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int blk = val[k] ? p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id[k] / p.cmp_bs] : -1;
+            val[k] = val[k] && blk >= 0;
+            coord[k] = val[k] ? blk * p.cmp_bs + id[k] % p.cmp_bs : 0;
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (val[k]) {
+            const uint8_t* rp = pool + (size_t)coord[k] * (D * 2);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) sas::prefetch_l2_line(rp + l * 128);
+          }
+        if (tracing) tr[TR_P_COORD] += clock64() - tc0;
+        const int slot = gchunk % CD;
+        if (!twait(&bars[B_CEMPTY + slot], ((gchunk / CD) & 1) ^ 1, abort_flag, p.status, 2, tracing,
+                   tr[TR_P_WAIT_MASK])) {
+          ok = false;
+          break;
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          coords[slot * CH + k * 32 + lane] = val[k] ? coord[k] : -1;
+          const unsigned vb = __ballot_sync(0xffffffffu, val[k]);
+          if (lane == 0) cmask[slot * 4 + k] = vb;
+        }
+        __syncwarp();
+        if (lane == 0) sas::mbar_arrive(&bars[B_CFULL + slot]);
+      }
+    }
+  } else if (warp < kLoaderWarps) {
+    // =============================== loaders (+ softmax group B, heads 32-63)
+    // Per chunk: copy the resolved rows, then do the softmax of the same chunk
+    // for heads 32-63 while its S^T is ready and before the next copies can
+    // start (they wait for this chunk's P.V). A segment's epilogue runs after
+    // the next segment's first copies have been issued.
     const int lw = warp;                // rows [32*lw, 32*lw+32) of every chunk
-    const int row = lw * 32 + lane;
     const int sub = lane >> 3, c16 = lane & 7;
     const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
+    SmGroup G{32, 1, lw, lane, lw * 32 + lane, lw == 0,
+              GroupSync{&bars[B_LSYNC], reinterpret_cast<uint32_t*>(misc + M_LWORD), 0}, 0.f,
+              tmem + ((uint32_t)(lw * 32) << 16), 0};
+    unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
-    wk.init(p.unit_start, p.T, p.R, r);
-    Seg sg;
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    Seg sg, pend;
+    bool have_pend = false;
     uint32_t gchunk = 0, seg_i = 0;
     const uint32_t q_bytes = (uint32_t)NSLAB * p.q_box_h * 128;
     bool ok = true;
     while (ok && wk.next(sg)) {
-      const TokInfo ti = p.tok[sg.t];
       if (tid == 0) {
         if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
           ok = false;
@@ -443,71 +971,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, sg.t);
         }
       }
-      // the compressed scan stops at the first -1 (golden.py:55-56): a range
-      // that starts inside a token looks for one in the slots before it
-      bool stopped = false;
-      const int cmp_c0 = max(sg.cb - p.n_win_chunks, 0);
-      if (p.scenario == 3 && cmp_c0 > 0) {
-        const int lim = min(cmp_c0 * CH, ti.n_cmp);
-        const int32_t* ip = p.idx + (size_t)sg.t * p.K;
-        int neg = 0;
-        for (int e = row; e < lim; e += kLoaderThreads) neg |= (ip[e] == -1);
-        stopped = sas::named_bar_or(3, kLoaderThreads, neg) != 0;
-      }
       for (int c = sg.cb; ok && c < sg.ce; ++c, ++gchunk) {
-        const long long tc0 = tracing ? clock64() : 0;
         const bool is_win = c < p.n_win_chunks;
-        long long coord = -1;  // physical row in the pool, -1 = masked
-        bool val;
-        if (is_win) {
-          const int lo = max(ti.s_g - p.win_left, 0);
-          const int pos = lo + c * CH + row;
-          val = (ti.s_g >= 0) && pos <= ti.s_g;
-          if (val) {
-            const int blk = p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs];
-            val = blk >= 0;
-            coord = (long long)blk * p.ori_bs + pos % p.ori_bs;
-          }
-        } else {
-          const int e = (c - p.n_win_chunks) * CH + row;
-          val = e < ti.n_cmp;
-          int id = e;
-          if (p.scenario == 3) {
-            id = val ? p.idx[(size_t)sg.t * p.K + e] : 0;
-            const unsigned bal = __ballot_sync(0xffffffffu, val && id == -1);
-            if (lane == 0) first_neg[(gchunk & 1) * 4 + lw] = bal ? lw * 32 + __ffs(bal) - 1 : CH;
-            sas::named_bar_sync(3, kLoaderThreads);
-            const int* fn = first_neg + (gchunk & 1) * 4;
-            const int cf = min(min(fn[0], fn[1]), min(fn[2], fn[3]));
-            val = val && !stopped && row < cf && id >= 0 && id < ti.thr;
-            stopped = stopped || cf < CH;
-          } else {
-            val = val && id < ti.thr;
-          }
-          if (val) {
-            const int blk = p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id / p.cmp_bs];
-            val = blk >= 0;
-            coord = (long long)blk * p.cmp_bs + id % p.cmp_bs;
-          }
-        }
-        if (!val) coord = -1;
-        if (tracing) tr[TR_P_COORD] += clock64() - tc0;
-        // ---- publish the validity mask of this chunk
-        const int mb = gchunk & 1;
-        if (!twait(&bars[B_MEMPTY + mb], ((gchunk >> 1) & 1) ^ 1, abort_flag, p.status, 2, tracing,
-                   tr[TR_P_WAIT_MASK])) {
+        const int slot = gchunk % CD;
+        if (!twait(&bars[B_CFULL + slot], (gchunk / CD) & 1, abort_flag, p.status, 3, tracing,
+                   tr[TR_P_WAIT_MASK])) {  // wait for the rows to be resolved
           ok = false;
           break;
         }
-        const unsigned vb = __ballot_sync(0xffffffffu, val);
-        if (lane == 0) {
-          mask_words[mb * 4 + lw] = vb;
-          sas::mbar_arrive(&bars[B_MFULL + mb]);
-        }
         // ---- rows this lane copies: 4 rows x 8 lanes x 16 B per instruction
-        long long crw[8];
+        int crw[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) crw[i] = __shfl_sync(0xffffffffu, coord, 4 * i + sub);
+        for (int i = 0; i < 8; ++i) crw[i] = coords[slot * CH + lw * 32 + 4 * i + sub];
+        const bool valid = (cmask[slot * 4 + lw] >> lane) & 1;
+        __syncwarp();
+        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + slot]);
         const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
         for (int s = 0; s < NSLAB; ++s) {
           if (!twait(&bars[B_EMPTY + s], (gchunk & 1) ^ 1, abort_flag, p.status, 3, tracing,
@@ -526,9 +1004,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           cp_async_arrive(&bars[B_FULL + s]);
         }
+        if (!ok) break;
+        if (have_pend) {
+          have_pend = false;
+          if (!segment_epilogue<DT>(p, G, sm, bars, pend, r, g, wk.u, abort_flag, false, trb)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!softmax_chunk<DT>(p, G, sm, bars, gchunk, c == sg.cb, valid, g, abort_flag, false, trb)) {
+          ok = false;
+          break;
+        }
       }
+      pend = sg;
+      have_pend = true;
       ++seg_i;
     }
+    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, pend, r, g, wk.u, abort_flag, false, trb);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     if (lane == 0) {
@@ -538,7 +1031,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
       const uint32_t p_base = sas::smem_u32(smem + OFF_P);
       Walker wk;
-      wk.init(p.unit_start, p.T, p.R, r);
+      wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
       Seg sg;
       uint32_t gchunk = 0, seg_i = 0;
       bool ok = true;
@@ -546,6 +1039,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!twait(&bars[B_QFULL], seg_i & 1, abort_flag, p.status, 4, tracing, tr[TR_M_WAIT_Q])) break;
         for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
           const bool first = c == sg.cb, last = c == sg.ce - 1;
+          long long tg0 = 0;
           // S^T = K . Q^T
           for (int s = 0; s < NSLAB; ++s) {
             if (!twait(&bars[B_FULL + s], gchunk & 1, abort_flag, p.status, 5, tracing, tr[TR_M_WAIT_FULL])) {
@@ -554,6 +1048,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
             sas::tc_fence_after();
+            if (tracing && s == 0) tg0 = clock64();
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = sas::umma_desc_sw128(kv_base + s * SLAB_BYTES + kk * 32, 16, 1024);
@@ -564,6 +1059,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           sas::umma_commit(&bars[B_SFULL]);
           if (last) sas::umma_commit(&bars[B_QEMPTY]);
+          if (tracing) {  // diagnostics only: G1 latency, first issue to completion
+            unsigned long long dummy = 0;
+            twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 4, false, dummy);
+            tr[TR_M_WAIT_O] += clock64() - tg0;
+          }
           // O^T += V^T . P^T
           if (!twait(&bars[B_PREADY], gchunk & 1, abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P])) {
             ok = false;
@@ -576,6 +1076,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           sas::tc_fence_after();
+          if (tracing) tg0 = clock64();
 #pragma unroll 1
           for (int j = 0; j < 4; ++j) {
 #pragma unroll
@@ -588,220 +1089,64 @@ __global__ void __launch_bounds__(kThreads, 1)
             sas::umma_commit(&bars[B_EMPTY + 2 * j + 1]);
           }
           if (last) sas::umma_commit(&bars[B_OFULL]);
+          if (tracing) {  // diagnostics only: G2 latency
+            unsigned long long dummy = 0;
+            twait(&bars[B_EMPTY + NSLAB - 1], gchunk & 1, abort_flag, p.status, 4, false, dummy);
+            tr[TR_E_COPY] += clock64() - tg0;
+          }
         }
         ++seg_i;
       }
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4) {
-    // =============================== softmax / epilogue (one thread per KV row)
-    using IO = IoType<DT>;
-    const int quad = warp & 3;          // TMEM lane quadrant of this warp
-    const int row = quad * 32 + lane;   // KV row of the chunk / d within an O^T tile
-    const int st = tid - kSoftmaxWarp0 * 32;  // 0..127
-    const uint32_t lane_addr = tmem + ((uint32_t)(quad * 32) << 16);
-    float lsum0 = 0.f, lsum1 = 0.f;  // running sums of heads 2*lane, 2*lane+1 over this warp's rows
+    // =============================== softmax group A (heads 0-31) / epilogue
+    const int quad = warp & 3;  // TMEM lane quadrant of this warp
+    SmGroup G{0, 0, quad, lane, quad * 32 + lane, quad == 0,
+              GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, 0.f,
+              tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
-    wk.init(p.unit_start, p.T, p.R, r);
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
-    uint32_t gchunk = 0, seg_i = 0;
+    uint32_t gchunk = 0;
     bool ok = true;
-    uint8_t* pbuf = smem + OFF_P;
     while (ok && wk.next(sg)) {
-      const int h0 = g * HG;
-      if (st < HG) {
-        const int h = h0 + st;
-        m_run[st] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
-      }
-      lsum0 = lsum1 = 0.f;
       for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
-        const bool first = c == sg.cb, last = c == sg.ce - 1;
-        const int mb = gchunk & 1;
-        if (!twait(&bars[B_MFULL + mb], (gchunk >> 1) & 1, abort_flag, p.status, 8, tracing, tr[TR_S_WAIT_MASK])) {
+        const int cslot = gchunk % CD;
+        if (!twait(&bars[B_CFULL + cslot], (gchunk / CD) & 1, abort_flag, p.status, 8, tracing,
+                   tr[TR_S_WAIT_MASK])) {
           ok = false;
           break;
         }
-        const bool valid = (mask_words[mb * 4 + (row >> 5)] >> (row & 31)) & 1;
-        sas::mbar_arrive(&bars[B_MEMPTY + mb]);
-        if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) {
+        const bool valid = (cmask[cslot * 4 + quad] >> lane) & 1;
+        __syncwarp();
+        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + cslot]);
+        if (!softmax_chunk<DT>(p, G, sm, bars, gchunk, c == sg.cb, valid, g, abort_flag, tracing, tr)) {
           ok = false;
           break;
         }
-        sas::tc_fence_after();
-        const long long ts0 = tracing ? clock64() : 0;
-        // ---- this row's scaled scores (log2 units), one TMEM read per chunk
-        float x[64];
-        {
-          uint32_t ra[32], rb[32];
-          sas::tmem_ld32(lane_addr + TM_S, ra);
-          sas::tmem_ld32(lane_addr + TM_S + 32, rb);
-          sas::tmem_wait_ld();
-#pragma unroll
-          for (int h = 0; h < 32; ++h) {
-            x[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
-            x[h + 32] = valid ? __uint_as_float(rb[h]) * p.scale_log2 : -INFINITY;
-          }
-        }
-        // ---- per-head max over the warp's 32 rows (redux), then over the 4 warps
-#pragma unroll
-        for (int h = 0; h < 64; h += 4) {
-          float4 w;
-          w.x = sas::warp_max_f32(x[h]);
-          w.y = sas::warp_max_f32(x[h + 1]);
-          w.z = sas::warp_max_f32(x[h + 2]);
-          w.w = sas::warp_max_f32(x[h + 3]);
-          if (lane == 0) *reinterpret_cast<float4*>(red + quad * 64 + h) = w;
-        }
-        sas::named_bar_sync(1, 128);
-        int need = 0;
-        if (st < HG) {
-          const float mx = fmaxf(fmaxf(red[st], red[64 + st]), fmaxf(red[128 + st], red[192 + st]));
-          const float mo = m_run[st];
-          float al = 1.f;
-          if (mx > mo + p.tau) {
-            al = sas::ex2(mo - mx);
-            m_run[st] = mx;
-            need = 1;
-          }
-          alpha_s[st] = al;
-        }
-        need = sas::named_bar_or(2, 128, need);
-        if (need) {
-          lsum0 *= alpha_s[2 * lane];
-          lsum1 *= alpha_s[2 * lane + 1];
-          if (!first) {
-#pragma unroll 1
-            for (int j = 0; j < 8; ++j) {
-              uint32_t o[32];
-              sas::tmem_ld32(lane_addr + TM_O + 32 * j, o);
-              sas::tmem_wait_ld();
-              const int hb = (j & 1) * 32;
-#pragma unroll
-              for (int h = 0; h < 32; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha_s[hb + h]);
-              sas::tmem_st32(lane_addr + TM_O + 32 * j, o);
-            }
-            sas::tmem_wait_st();
-          }
-        }
-        // ---- p = 2^(x - m) (masked rows give 0); P^T to smem (128 B rows,
-        // 128B swizzle) rounded to the I/O dtype; l sums the unrounded p
-        {
-#pragma unroll
-          for (int h = 0; h < 64; ++h) x[h] = sas::ex2(x[h] - m_run[h]);
-          uint8_t* prow = pbuf + row * 128;
-#pragma unroll
-          for (int c16 = 0; c16 < 8; ++c16) {
-            const int h = c16 * 8;
-            *reinterpret_cast<uint4*>(prow + ((c16 ^ (row & 7)) << 4)) =
-                make_uint4(IO::pack(x[h], x[h + 1]), IO::pack(x[h + 2], x[h + 3]),
-                           IO::pack(x[h + 4], x[h + 5]), IO::pack(x[h + 6], x[h + 7]));
-          }
-          warp_reduce_scatter64<false>(x, lane);
-          lsum0 += x[0];
-          lsum1 += x[1];
-        }
-        sas::fence_proxy_async_smem();
-        sas::tc_fence_before();
-        sas::mbar_arrive(&bars[B_PREADY]);
-        if (tracing) {
-          tr[TR_S_SOFTMAX] += clock64() - ts0;
-          tr[TR_CHUNKS] += 1;
-        }
-
-        if (last) {
-          // ------------------------------ epilogue
-          if (!twait(&bars[B_OFULL], seg_i & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) {
-            ok = false;
-            break;
-          }
-          sas::tc_fence_after();
-          const long long te0 = tracing ? clock64() : 0;
-          red[quad * 64 + 2 * lane] = lsum0;
-          red[quad * 64 + 2 * lane + 1] = lsum1;
-          sas::named_bar_sync(1, 128);
-          if (st < HG) {
-            const int h = h0 + st;
-            const float L = red[st] + red[64 + st] + red[128 + st] + red[192 + st];
-            const float m = m_run[st];
-            if (sg.complete) {
-              const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
-              const float Lf = L + sas::ex2(sink - m);
-              inv_s[st] = 1.f / Lf;
-              if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
-            } else {
-              inv_s[st] = L > 0.f ? 1.f / L : 0.f;
-              const size_t slot = ((size_t)r * 2 + sg.which) * p.G + g;
-              p.part_lse[slot * HG + st] = L > 0.f ? m + __log2f(L) : -INFINITY;
-            }
-          }
-          sas::named_bar_sync(1, 128);
-          if (tracing) tr[TR_E_RED] += clock64() - te0;
-          if (sg.complete) {
-            // direct stores: lanes pair up (row, row^1); the even lane stores
-            // head h for both rows, the odd lane head h+32 (4-byte stores, two
-            // 64-byte runs per warp instruction; no shared-memory staging, which
-            // would compete with the next segment's MMA operand reads)
-            typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
-            const bool odd = lane & 1;
-            const int d_even = row & ~1;
-            for (int j = 0; j < 4; ++j) {
-              uint32_t oa[32], ob[32];
-              const long long tt0 = tracing ? clock64() : 0;
-              sas::tmem_ld32(lane_addr + TM_O + 64 * j, oa);
-              sas::tmem_ld32(lane_addr + TM_O + 64 * j + 32, ob);
-              sas::tmem_wait_ld();
-              const long long tt1 = tracing ? clock64() : 0;
-              if (tracing) tr[TR_E_TMEM] += tt1 - tt0;
-#pragma unroll
-              for (int h = 0; h < 32; ++h) {
-                const float v0 = __uint_as_float(oa[h]) * inv_s[h];
-                const float v1 = __uint_as_float(ob[h]) * inv_s[h + 32];
-                const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
-                const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
-                const int hh = h0 + (odd ? h + 32 : h);
-                if (hh < p.H)
-                  *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
-              }
-              if (tracing) tr[TR_E_STAGE] += clock64() - tt1;
-            }
-          } else {
-            const size_t slot = ((size_t)r * 2 + sg.which) * p.G + g;
-            float* po = p.part_o + slot * HG * D;
-            for (int j = 0; j < 4; ++j) {
-              uint32_t oa[32], ob[32];
-              sas::tmem_ld32(lane_addr + TM_O + 64 * j, oa);
-              sas::tmem_ld32(lane_addr + TM_O + 64 * j + 32, ob);
-              sas::tmem_wait_ld();
-#pragma unroll
-              for (int h = 0; h < 32; ++h) {
-                po[(size_t)h * D + j * 128 + row] = __uint_as_float(oa[h]) * inv_s[h];
-                po[(size_t)(h + 32) * D + j * 128 + row] = __uint_as_float(ob[h]) * inv_s[h + 32];
-              }
-            }
-          }
-          sas::tc_fence_before();
-          sas::mbar_arrive(&bars[B_OEMPTY]);
-          if (tracing) {
-            tr[TR_S_EPI] += clock64() - te0;
-            tr[TR_SEGS] += 1;
-          }
+        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, sg, r, g, wk.u, abort_flag, tracing, tr)) {
+          ok = false;
+          break;
         }
       }
-      ++seg_i;
     }
   }
 
-  if (tracing) {
+  if (TRACE) {
     unsigned long long* tp = p.trace + (size_t)blockIdx.x * TR_NSLOTS;
     if (tid == 0) {
-      tp[TR_P_COORD] = tr[TR_P_COORD];
       tp[TR_P_WAIT_EMPTY] = tr[TR_P_WAIT_EMPTY];
       tp[TR_P_WAIT_MASK] = tr[TR_P_WAIT_MASK];
+    } else if (tid == kCoordWarp * 32) {
+      tp[TR_P_COORD] = tr[TR_P_COORD];
+      tp[TR_P_ISSUE] = tr[TR_P_WAIT_MASK];  // the coordinate warp's wait for a free ring slot
     } else if (warp == kMmaWarp && lane == 0) {
       tp[TR_M_WAIT_Q] = tr[TR_M_WAIT_Q];
       tp[TR_M_WAIT_FULL] = tr[TR_M_WAIT_FULL];
       tp[TR_M_WAIT_P] = tr[TR_M_WAIT_P];
       tp[TR_M_WAIT_O] = tr[TR_M_WAIT_O];
+      tp[TR_E_COPY] = tr[TR_E_COPY];
     } else if (tid == kSoftmaxWarp0 * 32) {
       tp[TR_S_WAIT_MASK] = tr[TR_S_WAIT_MASK];
       tp[TR_S_WAIT_S] = tr[TR_S_WAIT_S];
@@ -813,8 +1158,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tp[TR_TOTAL] = clock64() - t_start;
       tp[TR_E_TMEM] = tr[TR_E_TMEM];
       tp[TR_E_STAGE] = tr[TR_E_STAGE];
-      tp[TR_E_COPY] = tr[TR_E_COPY];
       tp[TR_E_RED] = tr[TR_E_RED];
+      for (int i = TR_S_LD; i < TR_NSLOTS; ++i) tp[i] = tr[i];
     }
   }
   sas::tc_fence_before();
@@ -823,82 +1168,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas::tc_fence_after();
     sas::tmem_dealloc(tmem, TMEM_COLS);
   }
-}
-
-// --------------------------------------------------------------- combine
-// Grid (R, H): CTA (r, h) looks at the boundary of range r (unit r*u). If the
-// boundary cuts a token and is the first boundary inside it, the CTA merges
-// that token's partials for head h; 128 threads, 4 output columns each.
-template <int DT>
-__global__ void __launch_bounds__(128) sas_combine_kernel(const FwdParams p) {
-  using IO = IoType<DT>;
-  const int rb = blockIdx.x;
-  const int h = blockIdx.y;
-  if (h >= p.H || rb == 0) return;
-  const int U = p.unit_start[p.T];
-  const int u = (U + p.R - 1) / p.R;
-  const int b0 = rb * u;
-  if (b0 >= U) return;
-  int lo = 0, hi = p.T - 1;  // token holding unit b0: largest t with unit_start[t] <= b0
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.unit_start[mid] <= b0) lo = mid; else hi = mid - 1;
-  }
-  const int t = lo;
-  const int st = p.unit_start[t], n = p.unit_start[t + 1] - st;
-  if (b0 == st || (rb - 1) * u > st) return;  // not a cut, or an earlier boundary owns it
-  const int g = h / HG, hh = h % HG;
-  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + ((size_t)t * p.H + h) * D;
-  const int d4 = threadIdx.x;  // float4 column group
-  const int r0 = st / u, r1 = (st + n - 1) / u;
-  const float sink = p.sinks[h] * kLog2e;
-  constexpr int kMaxUnrolled = 8;
-  float lse_i[kMaxUnrolled];
-  size_t slot_i[kMaxUnrolled];
-  const int ns = r1 - r0 + 1;
-  float m = sink;
-  for (int i = 0; i < ns; ++i) {
-    const int rr = r0 + i;
-    const int which = (rr == r0 && rr * u < st) ? 1 : 0;
-    const size_t slot = ((size_t)rr * 2 + which) * p.G + g;
-    const float l = p.part_lse[slot * HG + hh];
-    if (i < kMaxUnrolled) {
-      lse_i[i] = l;
-      slot_i[i] = slot;
-    }
-    m = fmaxf(m, l);
-  }
-  float den = sas::ex2(sink - m);
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int i = 0; i < kMaxUnrolled; ++i) {
-    if (i < ns) {
-      const float w = sas::ex2(lse_i[i] - m);
-      den += w;
-      const float4 v = reinterpret_cast<const float4*>(p.part_o + (slot_i[i] * HG + hh) * D)[d4];
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-  }
-  for (int i = kMaxUnrolled; i < ns; ++i) {  // long splits (rare): no unrolling
-    const int rr = r0 + i;
-    const size_t slot = ((size_t)rr * 2) * p.G + g;
-    const float w = sas::ex2(p.part_lse[slot * HG + hh] - m);
-    den += w;
-    const float4 v = reinterpret_cast<const float4*>(p.part_o + (slot * HG + hh) * D)[d4];
-    acc.x += w * v.x;
-    acc.y += w * v.y;
-    acc.z += w * v.z;
-    acc.w += w * v.w;
-  }
-  const float id = 1.f / den;
-  uint2 o;
-  o.x = IO::pack(acc.x * id, acc.y * id);
-  o.y = IO::pack(acc.z * id, acc.w * id);
-  reinterpret_cast<uint2*>(outp)[d4] = o;
-  if (p.lse && threadIdx.x == 0) p.lse[(size_t)t * p.H + h] = (m + __log2f(den)) * kLn2;
 }
 
 // ------------------------------------------------------------- host side
@@ -933,12 +1202,31 @@ bool make_q_map(CUtensorMap* m, const void* base, int T, int H, int box_h, CUten
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Launch with programmatic stream serialization, so the kernel's prologue can
+// overlap the previous kernel on the stream (the kernel calls pdl_wait()
+// before reading what that kernel wrote).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Tuning / diagnostics knobs set through sas_fwd_set_option (process-wide).
 float g_tau = 8.0f;
 unsigned long long* g_trace = nullptr;
 
 struct WsLayout {
-  size_t tok, unit, po, pl, total;
+  size_t tok, unit, po, pl, cnt, total;
 };
 WsLayout ws_layout(int T, int H, int num_sms) {
   const int G = (H + HG - 1) / HG;
@@ -948,7 +1236,8 @@ WsLayout ws_layout(int T, int H, int num_sms) {
   w.unit = align_up(w.tok + sizeof(TokInfo) * (size_t)std::max(T, 1), 256);
   w.po = align_up(w.unit + sizeof(int32_t) * ((size_t)T + 1), 256);
   w.pl = align_up(w.po + sizeof(float) * (size_t)R * 2 * G * HG * D, 256);
-  w.total = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
+  w.cnt = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
+  w.total = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
   return w;
 }
 
@@ -1031,11 +1320,12 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.dtype_bytes = 2;
   pp.out = out;
   pp.lse = lse;
+  pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
+  pp.n_cnt = R * G * 2;
   if (stage_mask & SAS_STAGE_PLAN) {
-    sas_plan_kernel<<<1, 1024, 0, st>>>(pp);
-    if (cudaGetLastError() != cudaSuccess) return SAS_ERR_CUDA;
+    if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }
-  if (!(stage_mask & (SAS_STAGE_ATTENTION | SAS_STAGE_COMBINE))) return SAS_OK;
+  if (!(stage_mask & SAS_STAGE_ATTENTION)) return SAS_OK;
 
   const CUtensorMapDataType tdt = dtype == SAS_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -1074,6 +1364,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.unit_start = pp.unit_start;
   fp.part_o = reinterpret_cast<float*>(ws + wl.po);
   fp.part_lse = reinterpret_cast<float*>(ws + wl.pl);
+  fp.merge_cnt = pp.merge_cnt;
   fp.status = status;
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;
@@ -1081,26 +1372,26 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SAS_ERR_CUDA;
-  static uint64_t attr_done[2] = {0, 0};  // per dtype, bit per device
-  if (!(attr_done[dtype] & (1ull << dev))) {
-    const cudaError_t e = dtype == SAS_DTYPE_BF16
-        ? cudaFuncSetAttribute(sas_fwd_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES)
-        : cudaFuncSetAttribute(sas_fwd_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (e != cudaSuccess) return SAS_ERR_CUDA;
-    attr_done[dtype] |= 1ull << dev;
+  static uint64_t attr_done = 0;  // bit per device
+  if (!(attr_done & (1ull << dev))) {
+    const int a = cudaFuncAttributeMaxDynamicSharedMemorySize;
+    if (cudaFuncSetAttribute(sas_fwd_kernel<0, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess)
+      return SAS_ERR_CUDA;
+    attr_done |= 1ull << dev;
   }
   if (stage_mask & SAS_STAGE_ATTENTION) {
-    if (dtype == SAS_DTYPE_BF16)
-      sas_fwd_kernel<0><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, fp);
-    else
-      sas_fwd_kernel<1><<<R * G, kThreads, SMEM_BYTES, st>>>(tm_q, fp);
-    if (cudaGetLastError() != cudaSuccess) return SAS_ERR_CUDA;
-  }
-  if (stage_mask & SAS_STAGE_COMBINE) {
-    if (dtype == SAS_DTYPE_BF16)
-      sas_combine_kernel<0><<<dim3(R, num_heads), 128, 0, st>>>(fp);
-    else
-      sas_combine_kernel<1><<<dim3(R, num_heads), 128, 0, st>>>(fp);
+    const bool tr = fp.trace != nullptr;
+    const dim3 grid(R * G), block(kThreads);
+    const cudaError_t e =
+        dtype == SAS_DTYPE_BF16
+            ? (tr ? launch_pdl(sas_fwd_kernel<0, true>, grid, block, SMEM_BYTES, st, tm_q, fp)
+                  : launch_pdl(sas_fwd_kernel<0, false>, grid, block, SMEM_BYTES, st, tm_q, fp))
+            : (tr ? launch_pdl(sas_fwd_kernel<1, true>, grid, block, SMEM_BYTES, st, tm_q, fp)
+                  : launch_pdl(sas_fwd_kernel<1, false>, grid, block, SMEM_BYTES, st, tm_q, fp));
+    if (e != cudaSuccess) return SAS_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
 }

@@ -38,6 +38,7 @@ struct MetaArgs {
   int64_t pre_token, next_token, group, m_base, s2_base;
   int is_s1g, is_cfa, is_scfa, att_mode;
   int fast;  // row_info_fast applies (band mask, finite window, S1G layout)
+  int smem;  // dynamic shared memory of this launch, bytes
 };
 
 struct BatchInfo {
@@ -409,6 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas_metadata_kernel(MetaArgs A, long long* __restrict__ ws_arrays, int64_t* __restrict__ core_out,
                         int32_t* __restrict__ meta_out, int32_t* status) {
   extern __shared__ long long sh_arrays[];
+  sas::pdl_launch_dependents();  // the plan kernel that follows may start launching
 
   __shared__ long long s_max_cost;
   __shared__ int s_all_zero;
@@ -472,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // per-row cost cache for the serial walk, in shared memory after the batch arrays
     const size_t arr_bytes = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * (size_t)(B > 0 ? B : 1) + 1) : 0;
     int2* rc = nullptr;
-    if (A.fast && arr_bytes + (size_t)n_items * 32 * sizeof(int2) <= (size_t)kSmemCap)
+    if (A.fast && arr_bytes + 16 + (size_t)n_items * 32 * sizeof(int2) <= (size_t)A.smem)
       rc = reinterpret_cast<int2*>(reinterpret_cast<char*>(sh_arrays) + ((arr_bytes + 15) & ~(size_t)15));
     for (long long it = warp; it < n_items; it += kThreads / 32) {
       int64_t lo = 0, hi = B - 1;  // batch of this item: last b with item[b] <= it
@@ -646,7 +648,16 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   long long* arrays = static_cast<long long*>(workspace);
   int64_t* core_out = reinterpret_cast<int64_t*>(static_cast<char*>(workspace) +
                                                  align_up(sizeof(long long) * (kNumArrays * b1 + 1), 256));
-  const size_t smem = kSmemCap;
+  // dynamic shared memory: the batch arrays plus a row-cost cache sized from
+  // max_seqlen_q (the kernel skips the cache when the real rows do not fit),
+  // so a decode batch does not ask for the whole carve-out
+  size_t smem = kSmemCap;
+  if (max_seqlen_q > 0) {
+    const size_t arr = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * b1 + 1) + 16 : 0;
+    const size_t rows = max_seqlen_q > kSmallRows ? b1 * (((size_t)max_seqlen_q + 31) / 32) * 32 : 0;
+    smem = std::min((size_t)kSmemCap, align_up(arr + rows * sizeof(int2), 1024));
+  }
+  A.smem = (int)smem;
   if (smem > 48 * 1024) {
     int dev = 0;
     cudaGetDevice(&dev);

@@ -48,7 +48,7 @@ extern "C" {
 /* stage_mask bits of sas_sparse_attn_sharedkv_fwd (SAS_STAGE_ALL for a normal call) */
 #define SAS_STAGE_PLAN 1
 #define SAS_STAGE_ATTENTION 2
-#define SAS_STAGE_COMBINE 4
+#define SAS_STAGE_COMBINE 4 /* the split-KV merge runs inside the attention launch; kept for callers, no launch */
 #define SAS_STAGE_ALL 7
 
 /* Library version, for a loader to check it got the build it expects. */
@@ -122,9 +122,10 @@ int sas_metadata_noalloc(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
  *   metadata     int32[1024] from sas_metadata (or any producer of the contract)
  *   out          same shape/dtype as q;  lse [num_tokens, num_heads] fp32 (may be NULL)
  * scenario: 1 = SWA, 2 = CFA (dense compressed rows), 3 = SCFA (top-k).
- * stage_mask: which of the three launches to enqueue (SAS_STAGE_*); the
- * stages communicate through `workspace`, so a split call sequence must pass
- * the same arguments to every stage. SAS_STAGE_ALL is the normal call.
+ * stage_mask: which launches to enqueue (SAS_STAGE_PLAN, SAS_STAGE_ATTENTION;
+ * the attention launch also merges split tokens). The stages communicate
+ * through `workspace`, so a split call sequence must pass the same arguments
+ * to every stage. SAS_STAGE_ALL is the normal call.
  * ---------------------------------------------------------------------- */
 size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads, int32_t num_sms);
 

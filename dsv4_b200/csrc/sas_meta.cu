@@ -271,6 +271,61 @@ struct Arrays {
   }
 };
 
+// Smallest j in [lo, hi) with val(j) > x, for val non-decreasing on [lo, hi);
+// hi when there is none. One warp, 32 probes per round.
+template <typename I, typename F>
+__device__ __forceinline__ I warp_first_gt(const F& val, I lo, I hi, I x, int lane) {
+  while (hi > lo) {
+    const I step = (hi - lo + 31) / 32;
+    const I pk = lo + (I)(lane + 1) * step - 1;
+    const bool gt = pk >= hi || val(pk) > x;
+    const unsigned bal = __ballot_sync(0xffffffffu, gt);
+    if (bal == 0) return hi;
+    const int k0 = __ffs(bal) - 1;
+    const I p0 = lo + (I)(k0 + 1) * step - 1;
+    lo = lo + (I)k0 * step;
+    hi = p0 < hi ? p0 : hi;
+  }
+  return lo;
+}
+
+// Inclusive prefix sums of in[0, n) into out (a different array), by the
+// whole block: each thread sums a contiguous run, the runs are scanned
+// through shared memory, then each thread writes its run.
+template <typename F>
+__device__ void block_inclusive_prefix(const F& in, long long* out, int64_t n, long long* s_warp) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kWarps = kThreads / 32;
+  const int64_t per = (n + kThreads - 1) / kThreads;
+  const int64_t b0 = (int64_t)tid * per, b1 = b0 + per < n ? b0 + per : n;
+  long long local = 0;
+  for (int64_t b = b0; b < b1; ++b) local += in(b);
+  long long incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    long long w = lane < kWarps ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long u = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += u;
+    }
+    if (lane < kWarps) s_warp[lane] = w;
+  }
+  __syncthreads();
+  long long run = (warp ? s_warp[warp - 1] : 0) + incl - local;
+  for (int64_t b = b0; b < b1; ++b) {
+    run += in(b);
+    out[b] = run;
+  }
+  __syncthreads();
+}
+
 template <typename I>
 struct RowT {
   I cost, block, lbc, s2_start;
@@ -290,7 +345,8 @@ __device__ __forceinline__ I warp_scan_t(I v, int lane) {
 // which halves the shuffle chain of the serial walk; else long long.
 template <typename I>
 __device__ void assign_cores(const MetaArgs& A, const Arrays& V, int64_t B, int64_t total, long long max_cost,
-                             int lane, int64_t* core_out, bool& overrun, int64_t& used, const int2* rc) {
+                             int lane, int64_t* core_out, bool& overrun, int64_t& used, const int2* rc,
+                             const long long* pitem, const long long* pcost) {
       const I max_s1g_cost = (I)max_cost;
   I cur_b = 0, cur_bn2 = 0, cur_s1g = 0, cur_s2 = 0, cur_core = 0;
   I unassigned = (I)total;
@@ -308,39 +364,58 @@ __device__ void assign_cores(const MetaArgs& A, const Arrays& V, int64_t B, int6
     const I limit = avg > max_s1g_cost ? avg : max_s1g_cost;
     I core_cost = 0;
     // AssignByBatch (718-745): the current bn2 is tested with its remaining
-    // cost, every following bn2 with its batch's full cost; 32 at a time.
+    // cost, every following bn2 with its batch's full cost. With P the
+    // inclusive prefix of bn2 costs, bn2 j >= base stops the walk when
+    // c_j != 0 and P(j) - lbc_j/2 > thr := limit - core_cost + P(base-1).
+    // Since lbc_j <= c_j, every non-empty j after the first j with
+    // P(j) > thr stops it too, so the stop is that j or the next non-empty
+    // one: two prefix searches instead of a walk.
     if (bn2_cost == 0 || limit + ((I)V.lbc[cur_b] >> 1) >= core_cost + bn2_cost) {
       core_cost += bn2_cost;
-      I base = cur_bn2 + 1;
-      while (true) {
+      const I nkv = (I)A.nkv;
+      auto pbn = [&](I j) -> I {  // inclusive prefix of bn2 costs
+        if (nkv == 1) return (I)pcost[j];
+        const I b = j / nkv;
+        return nkv * (b > 0 ? (I)pcost[b - 1] : (I)0) + (j - b * nkv + 1) * (I)V.cost[b];
+      };
+      const I base = cur_bn2 + 1;
+      const I pb0 = pbn(base - 1);
+      const I thr = limit - core_cost + pb0;
+      // the first 32 bn2s directly (the usual case), the rest by search
+      I jf;
+      {
         const I j = base + lane;
-        const bool end = j >= nbn2;
-        const I bj = end ? 0 : (A.nkv == 1 ? j : j / (I)A.nkv);
-        const I cj = end ? 0 : (I)V.cost[bj];
-        const I incl = warp_scan_t<I>(cj, lane);
-        const I excl = incl - cj;
-        const bool okj = end || cj == 0 || limit + ((I)V.lbc[bj] >> 1) >= core_cost + excl + cj;
-        const unsigned stop = __ballot_sync(0xffffffffu, end || !okj);
-        if (stop) {
-          const int f = __ffs(stop) - 1;
-          core_cost += __shfl_sync(0xffffffffu, excl, f);
-          if (__shfl_sync(0xffffffffu, (int)end, f)) {
-            cur_bn2 = nbn2;
-            cur_s1g = 0;
-            cur_s2 = 0;
-            finished = true;
-          } else {
-            cur_bn2 = base + f;
-            cur_b = __shfl_sync(0xffffffffu, bj, f);
-            bn2_cost = __shfl_sync(0xffffffffu, cj, f);
-            cur_s1g = 0;
-            sc = RowT<I>{(I)V.r0c[cur_b], (I)V.r0b[cur_b], (I)V.r0l[cur_b], 0};
-            cur_s2 = 0;
-          }
-          break;
+        bool stop = j >= nbn2;
+        if (!stop) {
+          const I bj = nkv == 1 ? j : j / nkv;
+          stop = (I)V.cost[bj] != 0 && pbn(j) - ((I)V.lbc[bj] >> 1) > thr;
         }
-        core_cost += __shfl_sync(0xffffffffu, incl, 31);
-        base += 32;
+        const unsigned bal = __ballot_sync(0xffffffffu, stop);
+        if (bal) {
+          jf = base + (I)(__ffs(bal) - 1);
+          if (jf > nbn2) jf = nbn2;
+        } else {
+          jf = warp_first_gt<I>(pbn, base + 32, nbn2, thr, lane);
+          if (jf < nbn2) {
+            const I bj = nkv == 1 ? jf : jf / nkv;
+            if (!((I)V.cost[bj] != 0 && pbn(jf) - ((I)V.lbc[bj] >> 1) > thr))
+              jf = warp_first_gt<I>(pbn, jf + 1, nbn2, pbn(jf), lane);
+          }
+        }
+      }
+      core_cost += (jf > base ? pbn(jf - 1) : pb0) - pb0;  // the bn2s in [base, jf)
+      if (jf >= nbn2) {
+        cur_bn2 = nbn2;
+        cur_s1g = 0;
+        cur_s2 = 0;
+        finished = true;
+      } else {
+        cur_bn2 = jf;
+        cur_b = nkv == 1 ? jf : jf / nkv;
+        bn2_cost = (I)V.cost[cur_b];
+        cur_s1g = 0;
+        sc = RowT<I>{(I)V.r0c[cur_b], (I)V.r0b[cur_b], (I)V.r0l[cur_b], 0};
+        cur_s2 = 0;
       }
     }
     if (!finished) {
@@ -352,18 +427,55 @@ __device__ void assign_cores(const MetaArgs& A, const Arrays& V, int64_t B, int6
         bn2_cost = bn2_cost - sc.cost < 0 ? 0 : bn2_cost - sc.cost;
         I base = cur_s1g + 1;
         int64_t scanned = 0;
-        while (true) {
-          const int64_t row = (int64_t)base + lane;
-          RowT<I> r;
-          if (rc != nullptr && bi.s1g_base > kSmallRows && row < bi.s1g_base) {
-            // cached by the per-row pass; s2 start is always 0 on this path and a
-            // row has blocks exactly when its cost is non-zero
-            const int2 e = rc[V.item[cur_b] * 32 + row];
-            r = RowT<I>{(I)e.x, (I)(e.x != 0), (I)e.y, 0};
-          } else {
-            const RowInfo r64 = row_info(A, bi, row);
-            r = RowT<I>{(I)r64.cost, (I)r64.block, (I)r64.lbc, (I)r64.s2_start};
+        bool done = false;
+        if (rc != nullptr && bi.s1g_base > kSmallRows && (int64_t)base < bi.s1g_base) {
+          // cached rows [base, s1g_base): prefix search as in AssignByBatch
+          // (a row has blocks exactly when its cost is non-zero, and its lbc
+          // never exceeds its cost)
+          const long long it0 = V.item[cur_b];
+          auto pex = [&](long long it) -> long long { return pitem[it] - rc[it * 32 + 31].x; };
+          const long long b0x = pex(it0);
+          auto prow = [&](I row) -> I {  // inclusive prefix of the batch's row costs
+            const long long it = it0 + (row >> 5);
+            return (I)(pex(it) - b0x + rc[it * 32 + (row & 31)].x);
+          };
+          auto crow = [&](I row) -> I { return row > 0 ? prow(row) - prow(row - 1) : prow(row); };
+          const I end = (I)bi.s1g_base;
+          const I pr0 = prow(base - 1);
+          const I thr = limit - core_cost + pr0;
+          auto rfail = [&](I row) -> bool {
+            const I lbc = (I)rc[(it0 + (row >> 5)) * 32 + (row & 31)].y;
+            return crow(row) != 0 && prow(row) - (lbc >> 1) > thr;
+          };
+          I rf;
+          {
+            const I row = base + lane;
+            const unsigned bal = __ballot_sync(0xffffffffu, row < end && rfail(row));
+            if (bal) {
+              rf = base + (I)(__ffs(bal) - 1);
+            } else {
+              rf = warp_first_gt<I>(prow, base + 32 < end ? base + 32 : end, end, thr, lane);
+              if (rf < end && !rfail(rf)) rf = warp_first_gt<I>(prow, rf + 1, end, prow(rf), lane);
+            }
           }
+          const I took = (rf > base ? prow(rf - 1) : pr0) - pr0;
+          core_cost += took;
+          bn2_cost = bn2_cost - took < 0 ? 0 : bn2_cost - took;
+          if (rf < end) {
+            cur_s1g = rf;
+            const I c = crow(rf);
+            sc = RowT<I>{c, (I)(c != 0), (I)rc[(it0 + (rf >> 5)) * 32 + (rf & 31)].y, 0};
+            cur_s2 = 0;
+            done = true;
+          } else {
+            scanned = (int64_t)(end - base);
+            base = end;  // continue past the batch's rows (metadata.py walks on)
+          }
+        }
+        while (!done) {
+          const int64_t row = (int64_t)base + lane;
+          const RowInfo r64 = row_info(A, bi, row);
+          RowT<I> r{(I)r64.cost, (I)r64.block, (I)r64.lbc, (I)r64.s2_start};
           const bool considered = r.block != 0;
           const I c = considered ? r.cost : 0;
           const I incl = warp_scan_t<I>(c, lane);
@@ -473,9 +585,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const long long n_items = s_total_items;
     // per-row cost cache for the serial walk, in shared memory after the batch arrays
     const size_t arr_bytes = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * (size_t)(B > 0 ? B : 1) + 1) : 0;
+    // per row (prefix of the row costs within its 32-row item, lbc), then one
+    // inclusive prefix of item totals per item
     int2* rc = nullptr;
-    if (A.fast && arr_bytes + 16 + (size_t)n_items * 32 * sizeof(int2) <= (size_t)A.smem)
+    long long* pitem = nullptr;
+    if (A.fast && arr_bytes + 16 + (size_t)n_items * (32 * sizeof(int2) + sizeof(long long)) <= (size_t)A.smem) {
       rc = reinterpret_cast<int2*>(reinterpret_cast<char*>(sh_arrays) + ((arr_bytes + 15) & ~(size_t)15));
+      pitem = reinterpret_cast<long long*>(rc + n_items * 32);
+    }
     for (long long it = warp; it < n_items; it += kThreads / 32) {
       int64_t lo = 0, hi = B - 1;  // batch of this item: last b with item[b] <= it
       while (lo < hi) {
@@ -487,8 +604,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t row = (it - V.item[b]) * 32 + lane;
       RowInfo r{0, 0, 0, 0};
       if (row < bi.s1g_base) r = row_info(A, bi, row);
-      if (rc) rc[it * 32 + lane] = make_int2((int)r.cost, (int)r.lbc);
-      const int64_t cs = warp_sum(r.cost);
+      const int64_t incl = warp_incl_scan(r.cost, lane);
+      if (rc) rc[it * 32 + lane] = make_int2((int)incl, (int)r.lbc);
+      const int64_t cs = __shfl_sync(0xffffffffu, incl, 31);
       long long mx = r.cost;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -530,6 +648,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       V.r0b[b] = r0.block;
     }
     __syncthreads();
+    // inclusive prefix of the batch costs, into last_row's storage (dead now)
+    __shared__ long long s_scan[kThreads / 32];
+    block_inclusive_prefix([&](int64_t b) { return V.cost[b]; }, V.last_row, B, s_scan);
+    // row cache: inclusive prefix of the item totals (rc.x is the prefix within an item)
+    if (rc) block_inclusive_prefix([&](int64_t it) { return (long long)rc[it * 32 + 31].x; }, pitem, n_items, s_scan);
     // ---- phase 2: greedy assignment (metadata.py:898-923), warp 0
     if (warp == 0 && A.aic > 0) {
       int64_t total = 0;
@@ -538,9 +661,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool overrun = false;
       int64_t used = 1;
       if (A.fast && total < (1LL << 30) && s_max_cost < (1LL << 30) && B * A.nkv < (1LL << 30))
-        assign_cores<int>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc);
+        assign_cores<int>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc, pitem, V.last_row);
       else
-        assign_cores<long long>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc);
+        assign_cores<long long>(A, V, B, total, s_max_cost, lane, core_out, overrun, used, rc, pitem, V.last_row);
       if (overrun && lane == 0 && status) atomicCAS(status, 0, SAS_ERR_SCHED_OVERRUN);
       if (lane == 0) s_used = used;
     }
@@ -655,7 +778,7 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   if (max_seqlen_q > 0) {
     const size_t arr = B <= kSmemBatches ? sizeof(long long) * (kNumArrays * b1 + 1) + 16 : 0;
     const size_t rows = max_seqlen_q > kSmallRows ? b1 * (((size_t)max_seqlen_q + 31) / 32) * 32 : 0;
-    smem = std::min((size_t)kSmemCap, align_up(arr + rows * sizeof(int2), 1024));
+    smem = std::min((size_t)kSmemCap, align_up(arr + rows * sizeof(int2) + rows / 32 * sizeof(long long), 1024));
   }
   A.smem = (int)smem;
   if (smem > 48 * 1024) {

@@ -81,13 +81,15 @@ constexpr int M_ABORT = 260;
 constexpr int M_CMASK = 272;     // CD x 4 words: row-validity mask per ring slot
 constexpr int M_LWORD = 384;     // 3 words: group B (loader warps) OR
 constexpr int M_SWORD = 400;     // 3 words: group A (softmax warps) OR
-constexpr int M_RANGE = 416;     // RangeInfo of this CTA (4 ints)
+constexpr int M_RANGE = 416;     // RangeInfo of this CTA (5 ints)
 constexpr int M_RED = 512;       // 4 x 64 floats = 1 KB
 constexpr int M_MRUN = 1536;     // 64 floats
 constexpr int M_ALPHA = 1792;    // 64 floats
 constexpr int M_INV = 2048;      // 64 floats
 constexpr int M_COORD = 2304;    // CD x 128 int32: pool row per chunk row (-1 = masked)
-constexpr int MISC_BYTES = M_COORD + CD * CH * 4;
+constexpr int M_MW = M_COORD + CD * CH * 4;  // kTmemMergeMax x 64 floats: merge weights
+constexpr int kTmemMergeMax = 4;                 // pieces merged straight from TMEM (else via L2)
+constexpr int MISC_BYTES = M_MW + kTmemMergeMax * 64 * 4;
 constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES + 1024;  // + alignment slack
 
 // barrier indices
@@ -124,6 +126,9 @@ struct PlanParams {
   float* lse;
   int32_t* merge_cnt;   // [n_cnt] split-token arrival counters, zeroed here
   int n_cnt;
+  int R;                 // ranges (CTAs) per head group
+  int32_t* piece_start;  // [R+1] first piece of each token (piece mode only)
+  int32_t* mode;         // 0: equal unit ranges; 1: token pieces, one per CTA
 };
 
 struct FwdParams {
@@ -144,6 +149,8 @@ struct FwdParams {
   float* part_o;    // [R*2*G][64][512]
   float* part_lse;  // [R*2*G][64]
   int32_t* merge_cnt;  // [R*G*2]: arrivals per cut token, keyed by (first range, group, head half)
+  const int32_t* piece_start;  // [R+1], piece mode only
+  const int32_t* mode;         // written by the plan kernel
   int32_t* status;
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
@@ -201,6 +208,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
     s_lin[tid][1] = row[4] * smax + row[5];
   }
   __syncthreads();
+  int my_units = 0;  // units of token tid (first pass), for the piece split
   for (int t0 = 0; t0 < p.T; t0 += blockDim.x) {
     const int t = t0 + tid;
     int units = 0;
@@ -246,6 +254,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
           for (int h = 0; h < p.H; ++h) p.lse[(size_t)t * p.H + h] = 0.f;
       }
     }
+    if (t0 == 0) my_units = units;
     // block exclusive scan of units
     int v = units;
     for (int o = 1; o < 32; o <<= 1) {
@@ -270,6 +279,49 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
     __syncthreads();
   }
   if (tid == 0) p.unit_start[p.T] = s_carry;
+  // ---- piece mode: with fewer tokens than ranges, split every token into
+  // k_t = ceil(n_t / u) balanced pieces, u the smallest piece length with
+  // sum_t k_t <= R, and give each piece its own CTA (decode: all SMs busy and
+  // no CTA holds parts of two tokens). T < R <= 1024, so token t is thread t.
+  if (p.T < p.R) {
+    const int n = tid < p.T ? my_units : 0;
+    int mx = n;
+    for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    __syncthreads();
+    if (lane == 0) s_warp[warp] = mx;
+    __syncthreads();
+    mx = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = max(mx, s_warp[w]);
+    int lo = 1, hi = max(mx, 1);
+    while (lo < hi) {  // every thread runs the same search
+      const int mid = (lo + hi) >> 1;
+      int c = n > 0 ? (n + mid - 1) / mid : 0;
+      for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+      __syncthreads();
+      if (lane == 0) s_warp[warp] = c;
+      __syncthreads();
+      int tot = 0;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += s_warp[w];
+      if (tot <= p.R) hi = mid; else lo = mid + 1;
+    }
+    const int k = n > 0 ? (n + lo - 1) / lo : 0;
+    // exclusive scan of k over the (at most 1024) tokens
+    int v = k;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += u;
+    }
+    __syncthreads();
+    if (lane == 31) s_warp[warp] = v;
+    __syncthreads();
+    int off = 0;
+    for (int w = 0; w < warp; ++w) off += s_warp[w];
+    if (tid < p.T) p.piece_start[tid] = off + v - k;
+    if (tid == p.T) p.piece_start[p.T] = off + v - k;  // k = 0 here: the total
+    if (tid == 0) *p.mode = 1;
+  } else if (tid == 0) {
+    *p.mode = 0;
+  }
 }
 
 // ------------------------------------------------------- work enumeration
@@ -319,12 +371,31 @@ __device__ __forceinline__ int range_start(const int32_t* us, int T, int U, int 
 // A CTA's unit range [u0, end) and the token holding u0, computed once per
 // CTA by one warp and shared through shared memory.
 struct RangeInfo {
-  int u0, end, t, u;
+  int u0, end, t, u, pieces;
 };
 
-__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, int T, int R, int r, int lane) {
+__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, const int32_t* ps, int mode, int T, int R,
+                                                   int r, int lane) {
   RangeInfo ri;
   const int U = us[T];
+  if (mode == 1) {
+    // piece mode: CTA r takes piece j of token t, units [st + j*n/k, st + (j+1)*n/k)
+    ri.pieces = 1;
+    ri.u = 0;
+    if (r >= ps[T]) {
+      ri.u0 = ri.end = U;
+      ri.t = T - 1;
+      return ri;
+    }
+    const int t = warp_last_le(ps, T, r, lane);
+    const int j = r - ps[t], k = ps[t + 1] - ps[t];
+    const int st = us[t], n = us[t + 1] - st;
+    ri.u0 = st + (int)((long long)j * n / k);
+    ri.end = st + (int)((long long)(j + 1) * n / k);
+    ri.t = t;
+    return ri;
+  }
+  ri.pieces = 0;
   ri.u = (U + R - 1) / R;
   ri.u0 = range_start(us, T, U, ri.u, r, lane);
   ri.end = r + 1 >= R ? U : range_start(us, T, U, ri.u, r + 1, lane);
@@ -489,12 +560,14 @@ struct SmShared {
 // Phase 2: every thread owns one float4 column and accumulates 8 heads at a
 // time, so 8 independent loads are in flight per partial. Partials come
 // from other CTAs, so they are read through L2 (.cg).
-__device__ __forceinline__ size_t part_slot(const FwdParams& p, int rr, int r0, int ust, int u, int g) {
-  return ((size_t)rr * 2 + ((rr == r0 && rr * u < ust) ? 1 : 0)) * p.G + g;
+// Workspace slot of range rr's partial of a cut token whose first range is r0;
+// wf = 1 when that token is not the first segment of range r0.
+__device__ __forceinline__ size_t part_slot(const FwdParams& p, int rr, int r0, int wf, int g) {
+  return ((size_t)rr * 2 + (rr == r0 ? wf : 0)) * p.G + g;
 }
 
 template <int DT>
-__device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g, int r0, int r1, int ust, int u,
+__device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g, int r0, int r1, int wf,
                                                 SmGroup& G, float* lse_s, volatile int* abort_flag) {
   using IO = IoType<DT>;
   const int ns = r1 - r0 + 1;
@@ -504,7 +577,7 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
     const int c = G.hb + G.gst, h = g * HG + c;
     float m = p.sinks[h] * kLog2e, den = 1.f;
     for (int i = 0; i < ns; ++i) {
-      const float l = __ldcg(p.part_lse + part_slot(p, r0 + i, r0, ust, u, g) * HG + c);
+      const float l = __ldcg(p.part_lse + part_slot(p, r0 + i, r0, wf, g) * HG + c);
       const float mn = fmaxf(m, l);
       den = den * sas::ex2(m - mn) + sas::ex2(l - mn);
       m = mn;
@@ -523,7 +596,7 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
     for (int j = 0; j < kHB; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
     for (int i = 0; i < ns; ++i) {
-      const size_t slot = part_slot(p, r0 + i, r0, ust, u, g);
+      const size_t slot = part_slot(p, r0 + i, r0, wf, g);
       const float* pl = p.part_lse + slot * HG + h0;
       const float4* po = reinterpret_cast<const float4*>(p.part_o + (slot * HG + h0) * D) + G.gst;
       float4 v[kHB];
@@ -678,14 +751,85 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
   return true;
 }
 
+// Merge of a cut token for the group's heads, run by the piece that lands
+// last, with its own piece straight from TMEM: the other pieces' normalised
+// partials (o_i, lse_i) are read through L2, its own is O/l in registers,
+// bit-identical to the partial it would have written. Every piece enters the
+// same way in range order, so the result does not depend on which piece
+// merges: lse = log2(2^sink + sum_i 2^lse_i), out = sum_i 2^(lse_i - lse) o_i.
+template <int DT>
+__device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, const SmShared& S, float* mw,
+                                                int t, int g, int r0, int r1, int wf, int own_r,
+                                                volatile int* abort_flag) {
+  using IO = IoType<DT>;
+  const int np = r1 - r0 + 1;  // <= kTmemMergeMax
+  if (G.gst < 32) {
+    const int c = G.hb + G.gst, h = g * HG + c;
+    const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
+    const float own = L > 0.f ? S.m_run[c] + __log2f(L) : -INFINITY;  // as the partial's lse
+    const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
+    float li[kTmemMergeMax];
+    float M = sink;
+    for (int i = 0; i < np; ++i) {
+      const int rr = r0 + i;
+      li[i] = rr == own_r ? own : __ldcg(p.part_lse + part_slot(p, rr, r0, wf, g) * HG + c);
+      M = fmaxf(M, li[i]);
+    }
+    float den = sas::ex2(sink - M);
+    for (int i = 0; i < np; ++i) den += sas::ex2(li[i] - M);
+    const float lse = M + __log2f(den);
+    for (int i = 0; i < np; ++i) mw[i * 64 + c] = sas::ex2(li[i] - lse);
+    if (p.lse && h < p.H) p.lse[(size_t)t * p.H + h] = lse * kLn2;
+  }
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 23)) return false;
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)t * p.H * D;
+  const int row = G.gst;
+  const bool odd = G.lane & 1;
+  const int d_even = row & ~1;
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    float acc[32];
+#pragma unroll
+    for (int h = 0; h < 32; ++h) acc[h] = 0.f;
+#pragma unroll 1
+    for (int i = 0; i < np; ++i) {
+      const int rr = r0 + i;
+      float v[32];
+      if (rr == own_r) {
+        uint32_t o[32];
+        sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+        sas::tmem_wait_ld();
+#pragma unroll
+        for (int h = 0; h < 32; ++h) v[h] = __fmul_rn(__uint_as_float(o[h]), S.inv[G.hb + h]);  // as written
+      } else {
+        const float* src = p.part_o + part_slot(p, rr, r0, wf, g) * HG * D + (size_t)G.hb * D + j * 128 + row;
+#pragma unroll
+        for (int h = 0; h < 32; ++h) v[h] = __ldcg(src + (size_t)h * D);
+      }
+#pragma unroll
+      for (int h = 0; h < 32; ++h) acc[h] = __fmaf_rn(mw[i * 64 + G.hb + h], v[h], acc[h]);
+    }
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      const float recv = __shfl_xor_sync(0xffffffffu, odd ? acc[h] : acc[h + 16], 1);
+      const uint32_t w = odd ? IO::pack(recv, acc[h + 16]) : IO::pack(acc[h], recv);
+      const int hh = g * HG + G.hb + (odd ? h + 16 : h);
+      if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+    }
+  }
+  return true;
+}
+
 // Epilogue of one segment for the group's heads: l over the 4 quads, then
-// out = O/l with the sink folded into l (complete token) or a normalised
-// partial (o, lse2) for a token cut across ranges; the group that lands a cut
-// token's last partial merges all of them.
+// out = O/l with the sink folded into l (complete token), or, for a token cut
+// across CTAs, the split-KV protocol: every piece but the last to finish
+// leaves a normalised partial (o, lse2); the last merges them. If all other
+// pieces are already in when a CTA gets here, it merges from its own TMEM and
+// never writes its partial.
 template <int DT>
 __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
-                                                 const Seg& sg, int r, int g, int u, volatile int* abort_flag,
-                                                 bool tracing, unsigned long long* tr) {
+                                                 float* mw, const Seg& sg, int r, int g, const RangeInfo& ri,
+                                                 volatile int* abort_flag, bool tracing, unsigned long long* tr) {
   using IO = IoType<DT>;
   if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
   sas::tc_fence_after();
@@ -704,10 +848,26 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
       if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
     } else {
       S.inv[c] = L > 0.f ? 1.f / L : 0.f;
-      p.part_lse[pslot * HG + c] = L > 0.f ? m + __log2f(L) : -INFINITY;
     }
   }
-  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 19)) return false;
+  // the ranges holding the token's pieces: r0 .. r1 (wf: r0 holds an earlier token first)
+  int r0 = r, r1 = r, wf = 0;
+  int32_t* cnt = nullptr;
+  int early = 0;
+  if (!sg.complete) {
+    if (ri.pieces) {
+      r0 = p.piece_start[sg.t];
+      r1 = p.piece_start[sg.t + 1] - 1;
+    } else {
+      const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
+      r0 = ust / ri.u;
+      r1 = (ust + un - 1) / ri.u;
+      wf = r0 * ri.u < ust ? 1 : 0;
+    }
+    cnt = p.merge_cnt + ((size_t)r0 * p.G + g) * 2 + G.half;
+    if (G.gst == 0 && r1 - r0 < kTmemMergeMax) early = atomicAdd(cnt, 0) == r1 - r0;
+  }
+  if (!G.gs.sync_or(early, G.lane, G.lead, early, abort_flag, p.status, 19)) return false;
   if (tracing) tr[TR_E_RED] += clock64() - te0;
   const int row = G.gst;  // d within an O^T tile
   if (sg.complete) {
@@ -732,7 +892,17 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
       }
     }
+  } else if (early) {
+    // every other piece is in: merge from TMEM, reset the counter for the next launch
+    __threadfence();
+    if (G.gst == 0) *cnt = 0;
+    if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
   } else {
+    if (G.gst < 32) {
+      const int c = G.hb + G.gst;
+      const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
+      p.part_lse[pslot * HG + c] = L > 0.f ? S.m_run[c] + __log2f(L) : -INFINITY;
+    }
     float* po = p.part_o + pslot * HG * D;
 #pragma unroll 1
     for (int j = 0; j < 4; ++j) {
@@ -740,31 +910,31 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
       sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
       sas::tmem_wait_ld();
 #pragma unroll
-      for (int h = 0; h < 32; ++h) po[(size_t)(G.hb + h) * D + j * 128 + row] = __uint_as_float(o[h]) * S.inv[G.hb + h];
+      for (int h = 0; h < 32; ++h)
+        po[(size_t)(G.hb + h) * D + j * 128 + row] = __fmul_rn(__uint_as_float(o[h]), S.inv[G.hb + h]);
     }
-  }
-  sas::tc_fence_before();
-  sas::mbar_arrive(&bars[B_OEMPTY]);
-  ++G.seg;
-  if (!sg.complete) {
-    // ---- fused split-KV merge: every range covering the token adds one
-    // arrival (per head half) to the counter of the token's first range
+    // every piece adds one arrival (per head half) to the counter of the
+    // token's first range; the one that lands last merges
     __threadfence();
     if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 20)) return false;
-    const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
-    const int r0 = ust / u, r1 = (ust + un - 1) / u;
     int mine = 0, is_last = 0;
     if (G.gst == 0) {
-      int32_t* cnt = p.merge_cnt + ((size_t)r0 * p.G + g) * 2 + G.half;
       mine = atomicAdd(cnt, 1) == r1 - r0;
       if (mine) *cnt = 0;  // every arrival is in: reset for the next launch
     }
     if (!G.gs.sync_or(mine, G.lane, G.lead, is_last, abort_flag, p.status, 21)) return false;
     if (is_last) {
       __threadfence();
-      if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, ust, u, G, S.alpha, abort_flag)) return false;
+      if (r1 - r0 < kTmemMergeMax) {
+        if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
+      } else if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.alpha, abort_flag)) {
+        return false;
+      }
     }
   }
+  sas::tc_fence_before();
+  sas::mbar_arrive(&bars[B_OEMPTY]);
+  ++G.seg;
   if (tracing) {
     tr[TR_S_EPI] += clock64() - te0;
     tr[TR_SEGS] += 1;
@@ -791,6 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
   const SmShared sm{red, m_run, alpha_s, inv_s, smem + OFF_P};
+  float* mw = reinterpret_cast<float*>(misc + M_MW);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
@@ -832,7 +1003,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // everything above overlaps the plan kernel; its outputs are read below
   sas::pdl_wait();
   if (warp == 0) {
-    const RangeInfo ri = compute_range(p.unit_start, p.T, p.R, r, lane);
+    const RangeInfo ri = compute_range(p.unit_start, p.piece_start, *p.mode, p.T, p.R, r, lane);
     if (lane == 0) *reinterpret_cast<RangeInfo*>(misc + M_RANGE) = ri;
   }
   if (tid == 32) sas::tma_prefetch_desc(&tm_q);
@@ -840,6 +1011,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sas::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const RangeInfo rinfo = *reinterpret_cast<const RangeInfo*>(misc + M_RANGE);
   constexpr bool tracing = TRACE;
   unsigned long long tr[TR_NSLOTS];
 #pragma unroll
@@ -853,7 +1025,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and the validity mask into the ring, and starts each valid row on its
     // way into L2, so the loaders' copies later hit L2.
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(p.unit_start, rinfo);
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
@@ -955,7 +1127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem + ((uint32_t)(lw * 32) << 16), 0};
     unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(p.unit_start, rinfo);
     Seg sg, pend;
     bool have_pend = false;
     uint32_t gchunk = 0, seg_i = 0;
@@ -1007,7 +1179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         if (have_pend) {
           have_pend = false;
-          if (!segment_epilogue<DT>(p, G, sm, bars, pend, r, g, wk.u, abort_flag, false, trb)) {
+          if (!segment_epilogue<DT>(p, G, sm, bars, mw, pend, r, g, rinfo, abort_flag, false, trb)) {
             ok = false;
             break;
           }
@@ -1021,7 +1193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       have_pend = true;
       ++seg_i;
     }
-    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, pend, r, g, wk.u, abort_flag, false, trb);
+    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, mw, pend, r, g, rinfo, abort_flag, false, trb);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     if (lane == 0) {
@@ -1031,7 +1203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
       const uint32_t p_base = sas::smem_u32(smem + OFF_P);
       Walker wk;
-      wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+      wk.init(p.unit_start, rinfo);
       Seg sg;
       uint32_t gchunk = 0, seg_i = 0;
       bool ok = true;
@@ -1106,7 +1278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, 0.f,
               tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(p.unit_start, rinfo);
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
@@ -1125,7 +1297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, sg, r, g, wk.u, abort_flag, tracing, tr)) {
+        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, mw, sg, r, g, rinfo, abort_flag, tracing, tr)) {
           ok = false;
           break;
         }
@@ -1226,7 +1398,7 @@ float g_tau = 8.0f;
 unsigned long long* g_trace = nullptr;
 
 struct WsLayout {
-  size_t tok, unit, po, pl, cnt, total;
+  size_t tok, unit, po, pl, cnt, ps, hdr, total;
 };
 WsLayout ws_layout(int T, int H, int num_sms) {
   const int G = (H + HG - 1) / HG;
@@ -1237,7 +1409,9 @@ WsLayout ws_layout(int T, int H, int num_sms) {
   w.po = align_up(w.unit + sizeof(int32_t) * ((size_t)T + 1), 256);
   w.pl = align_up(w.po + sizeof(float) * (size_t)R * 2 * G * HG * D, 256);
   w.cnt = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
-  w.total = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
+  w.ps = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
+  w.hdr = align_up(w.ps + sizeof(int32_t) * ((size_t)R + 1), 256);
+  w.total = w.hdr + 256;
   return w;
 }
 
@@ -1322,6 +1496,9 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.lse = lse;
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
+  pp.R = R;
+  pp.piece_start = reinterpret_cast<int32_t*>(ws + wl.ps);
+  pp.mode = reinterpret_cast<int32_t*>(ws + wl.hdr);
   if (stage_mask & SAS_STAGE_PLAN) {
     if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }
@@ -1365,6 +1542,8 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.part_o = reinterpret_cast<float*>(ws + wl.po);
   fp.part_lse = reinterpret_cast<float*>(ws + wl.pl);
   fp.merge_cnt = pp.merge_cnt;
+  fp.piece_start = pp.piece_start;
+  fp.mode = pp.mode;
   fp.status = status;
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;

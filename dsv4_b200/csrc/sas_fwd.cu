@@ -66,6 +66,10 @@ constexpr int kMmaWarp = 8;             // warp 8: TMEM owner and MMA issuer
 constexpr int kCoordWarp = 9;           // warp 9: row resolution + L2 prefetch, runs ahead
 constexpr int kThreads = 32 * 10;
 constexpr int CD = 4;                    // depth of the row-coordinate ring (chunks)
+// Chunks a token may hold beyond a range's length before it is cut across
+// ranges: a cut costs the partial write-back and the merge, about this many
+// chunks of work.
+constexpr int kCutCost = 3;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -81,7 +85,7 @@ constexpr int M_ABORT = 260;
 constexpr int M_CMASK = 272;     // CD x 4 words: row-validity mask per ring slot
 constexpr int M_LWORD = 384;     // 3 words: group B (loader warps) OR
 constexpr int M_SWORD = 400;     // 3 words: group A (softmax warps) OR
-constexpr int M_RANGE = 416;     // RangeInfo of this CTA (5 ints)
+constexpr int M_RANGE = 416;     // RangeInfo of this CTA (4 ints)
 constexpr int M_RED = 512;       // 4 x 64 floats = 1 KB
 constexpr int M_MRUN = 1536;     // 64 floats
 constexpr int M_ALPHA = 1792;    // 64 floats
@@ -126,9 +130,6 @@ struct PlanParams {
   float* lse;
   int32_t* merge_cnt;   // [n_cnt] split-token arrival counters, zeroed here
   int n_cnt;
-  int R;                 // ranges (CTAs) per head group
-  int32_t* piece_start;  // [R+1] first piece of each token (piece mode only)
-  int32_t* mode;         // 0: equal unit ranges; 1: token pieces, one per CTA
 };
 
 struct FwdParams {
@@ -149,8 +150,6 @@ struct FwdParams {
   float* part_o;    // [R*2*G][64][512]
   float* part_lse;  // [R*2*G][64]
   int32_t* merge_cnt;  // [R*G*2]: arrivals per cut token, keyed by (first range, group, head half)
-  const int32_t* piece_start;  // [R+1], piece mode only
-  const int32_t* mode;         // written by the plan kernel
   int32_t* status;
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
@@ -208,7 +207,6 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
     s_lin[tid][1] = row[4] * smax + row[5];
   }
   __syncthreads();
-  int my_units = 0;  // units of token tid (first pass), for the piece split
   for (int t0 = 0; t0 < p.T; t0 += blockDim.x) {
     const int t = t0 + tid;
     int units = 0;
@@ -254,7 +252,6 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
           for (int h = 0; h < p.H; ++h) p.lse[(size_t)t * p.H + h] = 0.f;
       }
     }
-    if (t0 == 0) my_units = units;
     // block exclusive scan of units
     int v = units;
     for (int o = 1; o < 32; o <<= 1) {
@@ -279,49 +276,6 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
     __syncthreads();
   }
   if (tid == 0) p.unit_start[p.T] = s_carry;
-  // ---- piece mode: with fewer tokens than ranges, split every token into
-  // k_t = ceil(n_t / u) balanced pieces, u the smallest piece length with
-  // sum_t k_t <= R, and give each piece its own CTA (decode: all SMs busy and
-  // no CTA holds parts of two tokens). T < R <= 1024, so token t is thread t.
-  if (p.T < p.R) {
-    const int n = tid < p.T ? my_units : 0;
-    int mx = n;
-    for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    __syncthreads();
-    if (lane == 0) s_warp[warp] = mx;
-    __syncthreads();
-    mx = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) mx = max(mx, s_warp[w]);
-    int lo = 1, hi = max(mx, 1);
-    while (lo < hi) {  // every thread runs the same search
-      const int mid = (lo + hi) >> 1;
-      int c = n > 0 ? (n + mid - 1) / mid : 0;
-      for (int o = 16; o; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-      __syncthreads();
-      if (lane == 0) s_warp[warp] = c;
-      __syncthreads();
-      int tot = 0;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += s_warp[w];
-      if (tot <= p.R) hi = mid; else lo = mid + 1;
-    }
-    const int k = n > 0 ? (n + lo - 1) / lo : 0;
-    // exclusive scan of k over the (at most 1024) tokens
-    int v = k;
-    for (int o = 1; o < 32; o <<= 1) {
-      const int u = __shfl_up_sync(0xffffffffu, v, o);
-      if (lane >= o) v += u;
-    }
-    __syncthreads();
-    if (lane == 31) s_warp[warp] = v;
-    __syncthreads();
-    int off = 0;
-    for (int w = 0; w < warp; ++w) off += s_warp[w];
-    if (tid < p.T) p.piece_start[tid] = off + v - k;
-    if (tid == p.T) p.piece_start[p.T] = off + v - k;  // k = 0 here: the total
-    if (tid == 0) *p.mode = 1;
-  } else if (tid == 0) {
-    *p.mode = 0;
-  }
 }
 
 // ------------------------------------------------------- work enumeration
@@ -351,10 +305,6 @@ __device__ __forceinline__ int warp_last_le(const int32_t* us, int T, int x, int
   return lo;
 }
 
-// Chunks a token may hold beyond a range's length before it is cut across
-// ranges: a cut costs the partial write-back and the merge, about this many
-// chunks of work.
-constexpr int kCutCost = 3;
 
 // First unit of range r: r*u, moved back to the start of the token holding
 // it unless that token is too long to keep whole (more than u + kCutCost
@@ -371,31 +321,12 @@ __device__ __forceinline__ int range_start(const int32_t* us, int T, int U, int 
 // A CTA's unit range [u0, end) and the token holding u0, computed once per
 // CTA by one warp and shared through shared memory.
 struct RangeInfo {
-  int u0, end, t, u, pieces;
+  int u0, end, t, u;
 };
 
-__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, const int32_t* ps, int mode, int T, int R,
-                                                   int r, int lane) {
+__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, int T, int R, int r, int lane) {
   RangeInfo ri;
   const int U = us[T];
-  if (mode == 1) {
-    // piece mode: CTA r takes piece j of token t, units [st + j*n/k, st + (j+1)*n/k)
-    ri.pieces = 1;
-    ri.u = 0;
-    if (r >= ps[T]) {
-      ri.u0 = ri.end = U;
-      ri.t = T - 1;
-      return ri;
-    }
-    const int t = warp_last_le(ps, T, r, lane);
-    const int j = r - ps[t], k = ps[t + 1] - ps[t];
-    const int st = us[t], n = us[t + 1] - st;
-    ri.u0 = st + (int)((long long)j * n / k);
-    ri.end = st + (int)((long long)(j + 1) * n / k);
-    ri.t = t;
-    return ri;
-  }
-  ri.pieces = 0;
   ri.u = (U + R - 1) / R;
   ri.u0 = range_start(us, T, U, ri.u, r, lane);
   ri.end = r + 1 >= R ? U : range_start(us, T, U, ri.u, r + 1, lane);
@@ -786,34 +717,39 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
   const int row = G.gst;
   const bool odd = G.lane & 1;
   const int d_even = row & ~1;
+  // 16 heads per pass keeps the accumulators, the loads and the own O^T
+  // values within the register budget of the epilogue
 #pragma unroll 1
-  for (int j = 0; j < 4; ++j) {
-    float acc[32];
+  for (int pass = 0; pass < 8; ++pass) {
+    const int j = pass >> 1, hs = (pass & 1) * 16;  // O^T tile, first head of the pass
+    float acc[16];
 #pragma unroll
-    for (int h = 0; h < 32; ++h) acc[h] = 0.f;
+    for (int h = 0; h < 16; ++h) acc[h] = 0.f;
 #pragma unroll 1
     for (int i = 0; i < np; ++i) {
       const int rr = r0 + i;
-      float v[32];
+      float v[16];
       if (rr == own_r) {
-        uint32_t o[32];
-        sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+        uint32_t o[16];
+        sas::tmem_ld16(G.lane_addr + TM_O + 64 * j + G.hb + hs, o);
         sas::tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 32; ++h) v[h] = __fmul_rn(__uint_as_float(o[h]), S.inv[G.hb + h]);  // as written
+        for (int h = 0; h < 16; ++h) v[h] = __fmul_rn(__uint_as_float(o[h]), S.inv[G.hb + hs + h]);  // as written
       } else {
-        const float* src = p.part_o + part_slot(p, rr, r0, wf, g) * HG * D + (size_t)G.hb * D + j * 128 + row;
+        const float* src =
+            p.part_o + part_slot(p, rr, r0, wf, g) * HG * D + (size_t)(G.hb + hs) * D + j * 128 + row;
 #pragma unroll
-        for (int h = 0; h < 32; ++h) v[h] = __ldcg(src + (size_t)h * D);
+        for (int h = 0; h < 16; ++h) v[h] = __ldcg(src + (size_t)h * D);
       }
 #pragma unroll
-      for (int h = 0; h < 32; ++h) acc[h] = __fmaf_rn(mw[i * 64 + G.hb + h], v[h], acc[h]);
+      for (int h = 0; h < 16; ++h) acc[h] = __fmaf_rn(mw[i * 64 + G.hb + hs + h], v[h], acc[h]);
     }
+    // lanes pair up (row, row^1): the even lane stores heads hs..hs+7, the odd one hs+8..hs+15
 #pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      const float recv = __shfl_xor_sync(0xffffffffu, odd ? acc[h] : acc[h + 16], 1);
-      const uint32_t w = odd ? IO::pack(recv, acc[h + 16]) : IO::pack(acc[h], recv);
-      const int hh = g * HG + G.hb + (odd ? h + 16 : h);
+    for (int h = 0; h < 8; ++h) {
+      const float recv = __shfl_xor_sync(0xffffffffu, odd ? acc[h] : acc[h + 8], 1);
+      const uint32_t w = odd ? IO::pack(recv, acc[h + 8]) : IO::pack(acc[h], recv);
+      const int hh = g * HG + G.hb + hs + (odd ? h + 8 : h);
       if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
     }
   }
@@ -828,8 +764,8 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
 // never writes its partial.
 template <int DT>
 __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
-                                                 float* mw, const Seg& sg, int r, int g, const RangeInfo& ri,
-                                                 volatile int* abort_flag, bool tracing, unsigned long long* tr) {
+                                                 const Seg& sg, int r, int g, volatile int* abort_flag, bool tracing,
+                                                 unsigned long long* tr) {
   using IO = IoType<DT>;
   if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
   sas::tc_fence_after();
@@ -855,15 +791,11 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   int32_t* cnt = nullptr;
   int early = 0;
   if (!sg.complete) {
-    if (ri.pieces) {
-      r0 = p.piece_start[sg.t];
-      r1 = p.piece_start[sg.t + 1] - 1;
-    } else {
-      const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
-      r0 = ust / ri.u;
-      r1 = (ust + un - 1) / ri.u;
-      wf = r0 * ri.u < ust ? 1 : 0;
-    }
+    const RangeInfo ri = *reinterpret_cast<const RangeInfo*>(reinterpret_cast<uint8_t*>(bars) - M_BAR + M_RANGE);
+    const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
+    r0 = ust / ri.u;
+    r1 = (ust + un - 1) / ri.u;
+    wf = r0 * ri.u < ust ? 1 : 0;
     cnt = p.merge_cnt + ((size_t)r0 * p.G + g) * 2 + G.half;
     if (G.gst == 0 && r1 - r0 < kTmemMergeMax) early = atomicAdd(cnt, 0) == r1 - r0;
   }
@@ -892,12 +824,12 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
       }
     }
-  } else if (early) {
-    // every other piece is in: merge from TMEM, reset the counter for the next launch
-    __threadfence();
-    if (G.gst == 0) *cnt = 0;
-    if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
   } else {
+    int tmem_merge = early;
+    if (early) {
+      // every other piece is in: reset the counter for the next launch
+      if (G.gst == 0) *cnt = 0;
+    } else {
     if (G.gst < 32) {
       const int c = G.hb + G.gst;
       const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
@@ -924,12 +856,18 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
     }
     if (!G.gs.sync_or(mine, G.lane, G.lead, is_last, abort_flag, p.status, 21)) return false;
     if (is_last) {
-      __threadfence();
       if (r1 - r0 < kTmemMergeMax) {
-        if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
-      } else if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.alpha, abort_flag)) {
-        return false;
+        tmem_merge = 1;
+      } else {
+        __threadfence();
+        if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.alpha, abort_flag)) return false;
       }
+    }
+    }
+    if (tmem_merge) {
+      __threadfence();
+      float* mw = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) - M_BAR + M_MW);
+      if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
     }
   }
   sas::tc_fence_before();
@@ -961,7 +899,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
   const SmShared sm{red, m_run, alpha_s, inv_s, smem + OFF_P};
-  float* mw = reinterpret_cast<float*>(misc + M_MW);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
@@ -1003,7 +940,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // everything above overlaps the plan kernel; its outputs are read below
   sas::pdl_wait();
   if (warp == 0) {
-    const RangeInfo ri = compute_range(p.unit_start, p.piece_start, *p.mode, p.T, p.R, r, lane);
+    const RangeInfo ri = compute_range(p.unit_start, p.T, p.R, r, lane);
     if (lane == 0) *reinterpret_cast<RangeInfo*>(misc + M_RANGE) = ri;
   }
   if (tid == 32) sas::tma_prefetch_desc(&tm_q);
@@ -1011,7 +948,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   sas::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const RangeInfo rinfo = *reinterpret_cast<const RangeInfo*>(misc + M_RANGE);
   constexpr bool tracing = TRACE;
   unsigned long long tr[TR_NSLOTS];
 #pragma unroll
@@ -1025,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and the validity mask into the ring, and starts each valid row on its
     // way into L2, so the loaders' copies later hit L2.
     Walker wk;
-    wk.init(p.unit_start, rinfo);
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
@@ -1127,7 +1063,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem + ((uint32_t)(lw * 32) << 16), 0};
     unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
-    wk.init(p.unit_start, rinfo);
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg, pend;
     bool have_pend = false;
     uint32_t gchunk = 0, seg_i = 0;
@@ -1179,7 +1115,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         if (have_pend) {
           have_pend = false;
-          if (!segment_epilogue<DT>(p, G, sm, bars, mw, pend, r, g, rinfo, abort_flag, false, trb)) {
+          if (!segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb)) {
             ok = false;
             break;
           }
@@ -1193,7 +1129,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       have_pend = true;
       ++seg_i;
     }
-    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, mw, pend, r, g, rinfo, abort_flag, false, trb);
+    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     if (lane == 0) {
@@ -1203,7 +1139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
       const uint32_t p_base = sas::smem_u32(smem + OFF_P);
       Walker wk;
-      wk.init(p.unit_start, rinfo);
+      wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
       Seg sg;
       uint32_t gchunk = 0, seg_i = 0;
       bool ok = true;
@@ -1278,7 +1214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, 0.f,
               tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
-    wk.init(p.unit_start, rinfo);
+    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
@@ -1297,7 +1233,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
-        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, mw, sg, r, g, rinfo, abort_flag, tracing, tr)) {
+        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, sg, r, g, abort_flag, tracing, tr)) {
           ok = false;
           break;
         }
@@ -1398,7 +1334,7 @@ float g_tau = 8.0f;
 unsigned long long* g_trace = nullptr;
 
 struct WsLayout {
-  size_t tok, unit, po, pl, cnt, ps, hdr, total;
+  size_t tok, unit, po, pl, cnt, total;
 };
 WsLayout ws_layout(int T, int H, int num_sms) {
   const int G = (H + HG - 1) / HG;
@@ -1409,9 +1345,7 @@ WsLayout ws_layout(int T, int H, int num_sms) {
   w.po = align_up(w.unit + sizeof(int32_t) * ((size_t)T + 1), 256);
   w.pl = align_up(w.po + sizeof(float) * (size_t)R * 2 * G * HG * D, 256);
   w.cnt = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
-  w.ps = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
-  w.hdr = align_up(w.ps + sizeof(int32_t) * ((size_t)R + 1), 256);
-  w.total = w.hdr + 256;
+  w.total = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
   return w;
 }
 
@@ -1496,9 +1430,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.lse = lse;
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
-  pp.R = R;
-  pp.piece_start = reinterpret_cast<int32_t*>(ws + wl.ps);
-  pp.mode = reinterpret_cast<int32_t*>(ws + wl.hdr);
+
   if (stage_mask & SAS_STAGE_PLAN) {
     if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }
@@ -1542,8 +1474,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.part_o = reinterpret_cast<float*>(ws + wl.po);
   fp.part_lse = reinterpret_cast<float*>(ws + wl.pl);
   fp.merge_cnt = pp.merge_cnt;
-  fp.piece_start = pp.piece_start;
-  fp.mode = pp.mode;
+
   fp.status = status;
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;

@@ -227,7 +227,17 @@ def make_case_torch(*, ctx, q_lens, H, K, bs=128, D=512, scenario=3, cmp_ratio=4
             if n:
                 table[b, :n] = perm[cur:cur + n]
             cur += n
-        pool = torch.randn((total, bsz, 1, D), generator=g, device=device, dtype=torch.float32).to(tdt)
+        per_block = bsz * D
+        if total * per_block <= (1 << 31):
+            pool = torch.randn((total, bsz, 1, D), generator=g, device=device, dtype=torch.float32).to(tdt)
+        else:
+            # large caches (long-context decode): fill in pieces of ~2 GB of fp32
+            pool = torch.empty((total, bsz, 1, D), device=device, dtype=tdt)
+            step = max(1, (1 << 29) // per_block)
+            for b0 in range(0, total, step):
+                n = min(step, total - b0)
+                pool[b0:b0 + n] = torch.randn((n, bsz, 1, D), generator=g, device=device,
+                                              dtype=torch.float32).to(tdt)
         return pool, table
 
     q = torch.randn((T, H, D), generator=g, device=device, dtype=torch.float32).to(tdt)

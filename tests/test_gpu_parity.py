@@ -105,6 +105,31 @@ def test_attention_c2_scale_sampled():
     U.check_close(out, ro, lse, rl, rows=toks, what="C2 sample")
 
 
+# Cases that cut tokens across CTAs (a token longer than a range plus the cut
+# cost is split at range boundaries), covering both split-KV merge paths:
+#  - 40 dense-CFA tokens of ~22 chunks over 148 ranges of ~7: each token cut
+#    into 3-5 pieces (merged from TMEM up to 4 pieces, through L2 beyond);
+#  - one long token among short ones: a 9-chunk SCFA token cut into a few
+#    ranges (merged from TMEM), and a 41-chunk CFA token cut into many ranges
+#    (merged through L2).
+SPLIT_CASES = [
+    (dict(ctx=[10000 + 37 * i for i in range(40)], q_lens=[1] * 40, H=64, K=0, scenario=2, seed=31),
+     [0, 13, 27, 39]),
+    (dict(ctx=[200] * 149 + [20000], q_lens=[1] * 150, H=64, K=1024, seed=32), [0, 77, 148, 149]),
+    (dict(ctx=[100] * 149 + [20000], q_lens=[1] * 150, H=64, K=0, scenario=2, seed=33), [0, 148, 149]),
+]
+
+
+@pytest.mark.parametrize("cfg,toks", SPLIT_CASES, ids=["long_tokens", "one_long_tmem", "one_long_l2"])
+def test_attention_split_tokens(cfg, toks):
+    case = U.build_case(cfg)
+    out, lse = U.run_api(case)
+    ro, rl = U.oracle_forward(case, tokens=toks)
+    U.check_close(out, ro, lse, rl, rows=toks, what=str(cfg)[:80])
+    out2, lse2 = U.run_api(case)
+    assert np.array_equal(out, out2) and np.array_equal(lse, lse2), "split-token merge is not deterministic"
+
+
 def test_bsnd_layout_and_return_types():
     from dsv4_b200 import sparse_attn_sharedkv
 

@@ -44,6 +44,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+FUSED_PLAN_MAX_TOKENS = 512  # token counts planned inside the attention kernel (csrc/sas_fwd.cu kFusedMaxT)
 METRIC = "decode µs/layer & HBM GB/s (% of 8 TB/s); prefill TFLOP/s; 1/2/4/8 GPU"
 UNIT = "query tokens/s"
 
@@ -515,7 +516,9 @@ def ours_arm(a, rank, world, local_rank):
                      "algorithmic_bytes_per_launch": work["bytes"], "kernel": "sas_fwd_kernel"},
         "e2e": {"value": tokens_all * a.steps / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
-        "gpu_launches": 4 * a.steps,
+        # our kernels per step: the scheduler and the attention kernel, plus
+        # the plan kernel when the token count is above the fused-plan limit
+        "gpu_launches": (2 if T <= FUSED_PLAN_MAX_TOKENS else 3) * a.steps,
         "clocks": clk.summary(),
     }
     if a.config == "C4":

@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(_HERE, "libsas_b200.so")
 
 SAS_OK = 0
 STAGE_PLAN, STAGE_ATTENTION, STAGE_COMBINE, STAGE_ALL = 1, 2, 4, 7
+FLAG_AFTER_METADATA = 8  # the preceding kernel on the stream is sas_metadata for the same call
 OPT_RESCALE_THRESHOLD, OPT_TRACE_BUFFER = 1, 2
 ERRORS = {
     1: "invalid argument",
@@ -79,13 +80,24 @@ class _DeviceState:
         self.device = device
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.ws = torch.empty(0, dtype=torch.uint8, device=device)
+        self.meta_ws = torch.empty(0, dtype=torch.uint8, device=device)
         props = torch.cuda.get_device_properties(device)
         self.num_sms = props.multi_processor_count
 
     def workspace(self, nbytes: int) -> torch.Tensor:
         if self.ws.numel() < nbytes:
-            self.ws = torch.empty(max(nbytes, 2 * self.ws.numel()), dtype=torch.uint8, device=self.device)
+            # zeroed: the split-token counters in it start at zero and every
+            # launch leaves them zero
+            self.ws = torch.zeros(max(nbytes, 2 * self.ws.numel()), dtype=torch.uint8, device=self.device)
         return self.ws
+
+    def meta_workspace(self, nbytes: int) -> torch.Tensor:
+        """The scheduler's own scratch: it may run concurrently with an
+        attention launch (SAS_FLAG_AFTER_METADATA), so it never shares the
+        attention workspace."""
+        if self.meta_ws.numel() < nbytes:
+            self.meta_ws = torch.empty(max(nbytes, 2 * self.meta_ws.numel()), dtype=torch.uint8, device=self.device)
+        return self.meta_ws
 
 
 _states: Dict[int, _DeviceState] = {}

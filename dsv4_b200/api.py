@@ -149,6 +149,12 @@ def sparse_attn_sharedkv(
         cmp_kv_dev = None
         cmp_bt = None
 
+    lib = _lib.lib()
+    st = _lib.state(dev)
+    # the workspace first: a first-use allocation zero-fills it with a kernel,
+    # which must not sit between the scheduler and the attention launch
+    ws = st.workspace(lib.sas_fwd_workspace_bytes(T1, N1, st.num_sms))
+    flags = 0
     if metadata is None:
         meta_kwargs = dict(
             num_heads_q=N1, num_heads_kv=N2, head_dim=D,
@@ -166,6 +172,9 @@ def sparse_attn_sharedkv(
         if scenario == 3:
             meta_kwargs["cmp_topk"] = K
         metadata = sparse_attn_sharedkv_metadata(**meta_kwargs)
+        # nothing is enqueued between it and the attention launch, which may
+        # then overlap it
+        flags = _lib.FLAG_AFTER_METADATA
     md = metadata.to(device=dev, dtype=torch.int32)
     assert md.numel() == SAS_META_SIZE, f"metadata must have {SAS_META_SIZE} int32 entries (got {md.numel()})"
     md = md.reshape(SAS_META_SIZE).contiguous()
@@ -173,10 +182,6 @@ def sparse_attn_sharedkv(
     out_flat = out.view(T1, N1, D) if out is not None else torch.empty((T1, N1, D), dtype=q.dtype, device=dev)
     lse_flat = lse_out.view(T1, N1) if lse_out is not None else torch.empty((T1, N1), dtype=torch.float32,
                                                                               device=dev)
-    lib = _lib.lib()
-    st = _lib.state(dev)
-    nbytes = lib.sas_fwd_workspace_bytes(T1, N1, st.num_sms)
-    ws = st.workspace(nbytes)
     stream = torch.cuda.current_stream(dev).cuda_stream
     rc = lib.sas_sparse_attn_sharedkv_fwd(
         q_flat.data_ptr(), T1, N1, D, dcode, 1 if layout_q == "TND" else 0, int(B), int(S), _lib.ptr(cu),
@@ -186,7 +191,7 @@ def sparse_attn_sharedkv(
         cmp_kv_dev.shape[1] if cmp_kv_dev is not None else 0, _lib.ptr(cmp_bt),
         cmp_bt.shape[1] if cmp_bt is not None else 0,
         _lib.ptr(idx_dev), int(K), sinks_dev.data_ptr(), md.data_ptr(), float(softmax_scale), int(cmp_ratio_eff),
-        int(ori_win_left), scenario, out_flat.data_ptr(), lse_flat.data_ptr(), st.num_sms, int(_stages),
+        int(ori_win_left), scenario, out_flat.data_ptr(), lse_flat.data_ptr(), st.num_sms, int(_stages) | flags,
         st.status.data_ptr(),
         ws.data_ptr(), ws.numel(), stream)
     if rc in (1, 2):

@@ -94,7 +94,16 @@ constexpr int M_COORD = 2304;    // CD x 128 int32: pool row per chunk row (-1 =
 constexpr int M_MW = M_COORD + CD * CH * 4;  // kTmemMergeMax x 64 floats: merge weights
 constexpr int kTmemMergeMax = 4;                 // pieces merged straight from TMEM (else via L2)
 constexpr int MISC_BYTES = M_MW + kTmemMergeMax * 64 * 4;
-constexpr int SMEM_BYTES = OFF_MISC + MISC_BYTES + 1024;  // + alignment slack
+constexpr int kFusedMaxT = 512;  // token plans built inside the attention kernel (no plan kernel)
+// fused plan region: TokInfo[kFusedMaxT], pid[kFusedMaxT], units[kFusedMaxT + 1], smax
+constexpr int OFF_PLAN = OFF_MISC + MISC_BYTES;
+constexpr int P_PID = kFusedMaxT * 16;
+constexpr int P_US = P_PID + kFusedMaxT * 4;
+constexpr int P_SMAX = P_US + (kFusedMaxT + 1) * 4;
+constexpr int PLAN_BYTES = (P_SMAX + 4 + 15) / 16 * 16;
+constexpr int SMEM_BYTES = OFF_PLAN + PLAN_BYTES + 1024;  // fused plan; + alignment slack
+constexpr int SMEM_BYTES_BASE = OFF_PLAN + 1024;           // plan kernel's plan: more L1 left
+static_assert(SMEM_BYTES <= 232448, "shared memory over the per-CTA limit");
 
 // barrier indices
 constexpr int B_FULL = 0;        // 8
@@ -153,6 +162,13 @@ struct FwdParams {
   int32_t* status;
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
+  // fused plan (T <= kFusedMaxT): the CTA builds the token plan itself and
+  // checks metadata coverage at output time
+  int fused, early;          // early: the preceding kernel is our metadata kernel
+  int B, S, layout;
+  const int32_t* cu;
+  const int32_t* seqused_kv;
+  const int32_t* meta;
   unsigned long long* trace; // optional per-CTA cycle counters (nullptr in production)
 };
 
@@ -374,6 +390,7 @@ struct IoType<0> {
     __nv_bfloat16 v = __float2bfloat16_rn(a);
     return *reinterpret_cast<uint16_t*>(&v);
   }
+  __device__ static T zero() { return __float2bfloat16_rn(0.f); }
 };
 template <>
 struct IoType<1> {
@@ -386,6 +403,7 @@ struct IoType<1> {
     __half v = __float2half_rn(a);
     return *reinterpret_cast<uint16_t*>(&v);
   }
+  __device__ static T zero() { return __float2half_rn(0.f); }
 };
 
 // Reduce 64 per-thread values across the 32 lanes of a warp; afterwards
@@ -483,6 +501,12 @@ struct SmShared {
   float* inv;     // [64] 1 / l
   uint8_t* pbuf;  // P^T: 128 rows x 64 heads, 128B-swizzled
 };
+
+// The token plan this CTA uses (from the 1024-aligned shared-memory base
+// that the barriers sit in): its own fused plan, or the plan kernel's.
+__device__ __forceinline__ const uint8_t* smem_base_of(const uint64_t* bars) {
+  return reinterpret_cast<const uint8_t*>(bars) - M_BAR - OFF_MISC;
+}
 
 // Split-KV merge of one cut token for the heads [hb, hb+32) of group g, run
 // by one softmax group of the CTA that wrote the token's last partial:
@@ -772,6 +796,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   const long long te0 = tracing ? clock64() : 0;
   S.red[G.quad * 64 + G.hb + G.lane] = G.lsum;
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 18)) return false;
+
   const size_t pslot = ((size_t)r * 2 + sg.which) * p.G + g;
   if (G.gst < 32) {
     const int c = G.hb + G.gst, h = g * HG + c;
@@ -792,7 +817,9 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   int early = 0;
   if (!sg.complete) {
     const RangeInfo ri = *reinterpret_cast<const RangeInfo*>(reinterpret_cast<uint8_t*>(bars) - M_BAR + M_RANGE);
-    const int ust = p.unit_start[sg.t], un = p.unit_start[sg.t + 1] - ust;
+    const int32_t* us = p.fused ? reinterpret_cast<const int32_t*>(smem_base_of(bars) + OFF_PLAN + P_US)
+                                : p.unit_start;
+    const int ust = us[sg.t], un = us[sg.t + 1] - ust;
     r0 = ust / ri.u;
     r1 = (ust + un - 1) / ri.u;
     wf = r0 * ri.u < ust ? 1 : 0;
@@ -880,9 +907,140 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   return true;
 }
 
+// Fused plan: metadata coverage (kernel.py:254-278 windows) is checked after
+// the fact. Every token with work was written as if covered; once the
+// metadata is complete, each softmax group walks its range again and zeroes
+// its heads of every token that no core window covers (the reference leaves
+// those zero). The piece that merges a cut token does this after its merge,
+// so an uncovered cut token ends zero whatever the order of the pieces.
+template <int DT>
+__device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us, const int32_t* pid,
+                               const int* s_smax, const RangeInfo& ri, int g, volatile int* abort_flag) {
+  using IO = IoType<DT>;
+  sas::pdl_wait();  // the metadata is complete and visible
+  const int smax = *s_smax;
+  int lin0 = 0, lin1 = 0;  // this thread's core window, if any
+  if (G.gst < SAS_AIC_CORE_NUM) {
+    const int32_t* row = p.meta + G.gst * 8;
+    if (row[0] != 0) {
+      lin0 = row[1] * smax + row[2];
+      lin1 = row[4] * smax + row[5];
+    }
+  }
+  Walker wk;
+  wk.init(us, ri);
+  Seg sg;
+  while (wk.next(sg)) {
+    const int q = pid[sg.t];
+    int covered;
+    if (!G.gs.sync_or(q >= lin0 && q < lin1, G.lane, G.lead, covered, abort_flag, p.status, 24)) return false;
+    if (covered) continue;
+    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
+    for (int h = 0; h < 32; ++h) {
+      const int hh = g * HG + G.hb + h;
+      if (hh < p.H)
+        for (int j = 0; j < 4; ++j) outp[(size_t)hh * D + j * 128 + G.gst] = IO::zero();
+    }
+    if (p.lse && G.gst < 32 && g * HG + G.hb + G.gst < p.H) p.lse[(size_t)sg.t * p.H + g * HG + G.hb + G.gst] = 0.f;
+  }
+  return true;
+}
+
+// The plan kernel's work for up to kFusedMaxT tokens, done by every CTA of
+// the attention kernel into its own shared memory: per-token info and the
+// exclusive scan of chunk units. Metadata coverage is not applied here (the
+// epilogue checks it before writing a token), so none of this reads the
+// metadata and it can run while the metadata kernel is still in flight.
+// Output rows of tokens without work are zeroed, each by one CTA.
+template <int DT>
+__device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_pid, int32_t* s_us, int* s_smax,
+                           int* s_wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  constexpr int kW = kThreads / 32;
+  // max_seq: the reference api's S_max (api.py:208-215 / 229)
+  int mx = 0;
+  if (p.layout == SAS_LAYOUT_TND) {
+    for (int b = tid; b < p.B; b += kThreads) mx = max(mx, p.cu[b + 1] - p.cu[b]);
+  } else {
+    mx = p.S;
+  }
+  for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_wsum[warp] = mx;
+  __syncthreads();
+  int smax = 0;
+  for (int w = 0; w < kW; ++w) smax = max(smax, s_wsum[w]);
+  // one thread per request (TND) or per token (BSND): no per-token search
+  auto plan_token = [&](int t, int b, int s, int act_q) {
+    TokInfo ti{b, 0, 0, 0};
+    int units = 0;
+    if (s < act_q && b < p.B) {
+      const int s_g = p.seqused_kv[b] - act_q + s;
+      const int thr = max(py_floordiv(s_g + 1, p.ratio), 0);
+      const int n_cmp = p.scenario == 3 ? min(p.K, thr) : (p.scenario == 2 ? thr : 0);
+      ti.s_g = s_g;
+      ti.n_cmp = n_cmp;
+      ti.thr = thr;
+      units = p.n_win_chunks + (n_cmp + CH - 1) / CH;
+    }
+    s_tok[t] = ti;
+    s_pid[t] = b * smax + s;
+    s_us[t] = units;
+  };
+  if (p.layout == SAS_LAYOUT_TND) {
+    for (int b = tid; b < p.B; b += kThreads) {
+      const int c0 = p.cu[b], c1 = min(p.cu[b + 1], p.T);
+      for (int t = c0; t < c1; ++t) plan_token(t, b, t - c0, c1 - c0);
+    }
+    // tokens past cu[B] (none for a well-formed batch) carry no work
+    for (int t = p.cu[p.B] + tid; t < p.T; t += kThreads) plan_token(t, p.B, 0, 0);
+  } else {
+    for (int t = tid; t < p.T; t += kThreads) {
+      const int b = t / p.S, s = t - b * p.S;
+      plan_token(t, b, s, p.cu ? p.cu[b + 1] - p.cu[b] : p.S);
+    }
+  }
+  __syncthreads();
+  // tokens without work keep zero output and LSE (golden.py leaves them zero)
+  for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
+    if (s_us[t] != 0) continue;
+    uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * 2);
+    for (int i = tid; i < p.H * D * 2 / 16; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
+    if (p.lse)
+      for (int h = tid; h < p.H; h += kThreads) p.lse[(size_t)t * p.H + h] = 0.f;
+  }
+  // exclusive scan of the units, in place: each thread a run of <= 2 tokens
+  constexpr int kPer = (kFusedMaxT + kThreads - 1) / kThreads;
+  const int b0 = tid * kPer;
+  int v[kPer];
+  int local = 0;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    v[i] = b0 + i < p.T ? s_us[b0 + i] : 0;
+    local += v[i];
+  }
+  int incl = local;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  __syncthreads();
+  if (lane == 31) s_wsum[warp] = incl;
+  __syncthreads();
+  int run = incl - local;
+  for (int w = 0; w < warp; ++w) run += s_wsum[w];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    if (b0 + i < p.T) s_us[b0 + i] = run;
+    run += v[i];
+  }
+  if (tid == kThreads - 1) s_us[p.T] = run;  // the total
+  if (tid == 0) *s_smax = smax;
+  __syncthreads();
+}
+
 // TRACE = true builds the diagnostics variant that accumulates per-role cycle
 // counters into p.trace; the production variant carries none of that state.
-template <int DT, bool TRACE>
+template <int DT, bool TRACE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -898,6 +1056,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* m_run = reinterpret_cast<float*>(misc + M_MRUN);
   float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
+  // the token plan: this CTA's own (FUSED) or the plan kernel's
+  TokInfo* s_tok = reinterpret_cast<TokInfo*>(smem + OFF_PLAN);
+  int32_t* s_us = reinterpret_cast<int32_t*>(smem + OFF_PLAN + P_US);
+  const int32_t* usp = FUSED ? s_us : p.unit_start;
+  const TokInfo* tokp = FUSED ? s_tok : p.tok;
   const SmShared sm{red, m_run, alpha_s, inv_s, smem + OFF_P};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -937,10 +1100,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     sas::tmem_alloc(tmem_slot, TMEM_COLS);
     sas::tmem_relinquish();
   }
-  // everything above overlaps the plan kernel; its outputs are read below
-  sas::pdl_wait();
+  // everything above overlaps the kernel before; in early mode (fused plan,
+  // the kernel before is our metadata kernel, which writes nothing read here)
+  // the metadata is only waited for when a token's output is written
+  if (!p.early) sas::pdl_wait();
+  if constexpr (FUSED)
+    fused_plan<DT>(p, s_tok, reinterpret_cast<int32_t*>(smem + OFF_PLAN + P_PID), s_us,
+                   reinterpret_cast<int*>(smem + OFF_PLAN + P_SMAX), reinterpret_cast<int*>(red));
   if (warp == 0) {
-    const RangeInfo ri = compute_range(p.unit_start, p.T, p.R, r, lane);
+    const RangeInfo ri = compute_range(usp, p.T, p.R, r, lane);
     if (lane == 0) *reinterpret_cast<RangeInfo*>(misc + M_RANGE) = ri;
   }
   if (tid == 32) sas::tma_prefetch_desc(&tm_q);
@@ -961,12 +1129,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and the validity mask into the ring, and starts each valid row on its
     // way into L2, so the loaders' copies later hit L2.
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
     while (ok && wk.next(sg)) {
-      const TokInfo ti = p.tok[sg.t];
+      const TokInfo ti = tokp[sg.t];
       // the compressed scan stops at the first -1 (golden.py:55-56): a range
       // that starts inside a token looks for one in the slots before it
       bool stopped = false;
@@ -1063,7 +1231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               tmem + ((uint32_t)(lw * 32) << 16), 0};
     unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg, pend;
     bool have_pend = false;
     uint32_t gchunk = 0, seg_i = 0;
@@ -1129,7 +1297,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       have_pend = true;
       ++seg_i;
     }
-    if (ok && have_pend) segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb);
+    if (ok && have_pend) ok = segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb);
+    if (FUSED && ok)
+      zero_uncovered<DT>(p, G, usp, reinterpret_cast<const int32_t*>(smem + OFF_PLAN + P_PID),
+                         reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
+                         *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     if (lane == 0) {
@@ -1139,7 +1311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
       const uint32_t p_base = sas::smem_u32(smem + OFF_P);
       Walker wk;
-      wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+      wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
       Seg sg;
       uint32_t gchunk = 0, seg_i = 0;
       bool ok = true;
@@ -1214,7 +1386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, 0.f,
               tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
-    wk.init(p.unit_start, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
     uint32_t gchunk = 0;
     bool ok = true;
@@ -1239,6 +1411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (FUSED && ok)
+      zero_uncovered<DT>(p, G, usp, reinterpret_cast<const int32_t*>(smem + OFF_PLAN + P_PID),
+                         reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
+                         *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   }
 
   if (TRACE) {
@@ -1406,6 +1582,12 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   char* ws = static_cast<char*>(workspace);
 
   const int G = (num_heads + HG - 1) / HG;
+  // fused plan for small token counts (decode); early start only when the
+  // caller guarantees the kernel before is sas_metadata of this call (the
+  // CTA that shares an SM with the scheduler starts when it ends; measured,
+  // that beats leaving the SM out of the grid)
+  const bool fused = num_tokens <= kFusedMaxT;
+  const bool early = fused && (stage_mask & SAS_FLAG_AFTER_METADATA);
   const int R = std::max(1, num_sms / G);
   const int n_win_chunks = (ori_win_left + 1 + CH - 1) / CH;
 
@@ -1431,7 +1613,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
 
-  if (stage_mask & SAS_STAGE_PLAN) {
+  if ((stage_mask & SAS_STAGE_PLAN) && !fused) {
     if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }
   if (!(stage_mask & SAS_STAGE_ATTENTION)) return SAS_OK;
@@ -1478,6 +1660,14 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.status = status;
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;
+  fp.fused = fused ? 1 : 0;
+  fp.early = early ? 1 : 0;
+  fp.B = batch;
+  fp.S = max_seqlen_q;
+  fp.layout = layout_q;
+  fp.cu = cu_seqlens_q;
+  fp.seqused_kv = seqused_kv;
+  fp.meta = metadata;
   fp.trace = g_trace;
 
   int dev = 0;
@@ -1485,22 +1675,29 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   static uint64_t attr_done = 0;  // bit per device
   if (!(attr_done & (1ull << dev))) {
     const int a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    if (cudaFuncSetAttribute(sas_fwd_kernel<0, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<0, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(sas_fwd_kernel<0, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, true, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, true, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, false, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess)
       return SAS_ERR_CUDA;
     attr_done |= 1ull << dev;
   }
   if (stage_mask & SAS_STAGE_ATTENTION) {
     const bool tr = fp.trace != nullptr;
     const dim3 grid(R * G), block(kThreads);
-    const cudaError_t e =
-        dtype == SAS_DTYPE_BF16
-            ? (tr ? launch_pdl(sas_fwd_kernel<0, true>, grid, block, SMEM_BYTES, st, tm_q, fp)
-                  : launch_pdl(sas_fwd_kernel<0, false>, grid, block, SMEM_BYTES, st, tm_q, fp))
-            : (tr ? launch_pdl(sas_fwd_kernel<1, true>, grid, block, SMEM_BYTES, st, tm_q, fp)
-                  : launch_pdl(sas_fwd_kernel<1, false>, grid, block, SMEM_BYTES, st, tm_q, fp));
+    using KernelFn = void (*)(const CUtensorMap, const FwdParams);
+    // [dtype][trace][fused]
+    static const KernelFn kernels[2][2][2] = {
+        {{sas_fwd_kernel<0, false, false>, sas_fwd_kernel<0, false, true>},
+         {sas_fwd_kernel<0, true, false>, sas_fwd_kernel<0, true, true>}},
+        {{sas_fwd_kernel<1, false, false>, sas_fwd_kernel<1, false, true>},
+         {sas_fwd_kernel<1, true, false>, sas_fwd_kernel<1, true, true>}}};
+    const KernelFn k = kernels[dtype == SAS_DTYPE_BF16 ? 0 : 1][tr ? 1 : 0][fused ? 1 : 0];
+    const cudaError_t e = launch_pdl(k, grid, block, fused ? SMEM_BYTES : SMEM_BYTES_BASE, st, tm_q, fp);
     if (e != cudaSuccess) return SAS_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;

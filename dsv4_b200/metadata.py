@@ -148,7 +148,7 @@ def sparse_attn_sharedkv_metadata(
     lib = _lib.lib()
     st = _lib.state(dev)
     nbytes = lib.sas_metadata_workspace_bytes(max(int(B), 1), int(aic_core_num))
-    ws = st.workspace(nbytes)
+    ws = st.meta_workspace(nbytes)
     if out is None:
         out = torch.empty(SAS_META_SIZE, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream

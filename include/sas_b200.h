@@ -50,6 +50,14 @@ extern "C" {
 #define SAS_STAGE_ATTENTION 2
 #define SAS_STAGE_COMBINE 4 /* the split-KV merge runs inside the attention launch; kept for callers, no launch */
 #define SAS_STAGE_ALL 7
+/* Flag for stage_mask: the kernel enqueued just before this call on the same
+ * stream is sas_metadata for the same arguments. The attention launch may then
+ * start before that kernel ends (it reads the metadata only when it writes a
+ * token's output), overlapping the scheduler with the attention work. Never
+ * set it when another kernel may run in between (for example the producer of
+ * q): the attention kernel would read its inputs too early. The two calls
+ * must use separate workspaces, since they may run at the same time. */
+#define SAS_FLAG_AFTER_METADATA 8
 
 /* Library version, for a loader to check it got the build it expects. */
 int sas_version(void);
@@ -125,7 +133,9 @@ int sas_metadata_noalloc(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
  * stage_mask: which launches to enqueue (SAS_STAGE_PLAN, SAS_STAGE_ATTENTION;
  * the attention launch also merges split tokens). The stages communicate
  * through `workspace`, so a split call sequence must pass the same arguments
- * to every stage. SAS_STAGE_ALL is the normal call.
+ * to every stage. SAS_STAGE_ALL is the normal call. The workspace must be
+ * zero-filled before its first use (its split-token counters start at zero;
+ * every launch leaves them zero).
  * ---------------------------------------------------------------------- */
 size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads, int32_t num_sms);
 

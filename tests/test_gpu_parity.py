@@ -130,6 +130,45 @@ def test_attention_split_tokens(cfg, toks):
     assert np.array_equal(out, out2) and np.array_equal(lse, lse2), "split-token merge is not deterministic"
 
 
+def _covered_tokens(md, cu):
+    """Tokens inside some enabled core window of the metadata (kernel.py:254-278)."""
+    fa = md[:36 * 8].reshape(36, 8)
+    ql = np.diff(cu)
+    smax = int(ql.max())
+    wins = [(int(r[1]) * smax + int(r[2]), int(r[4]) * smax + int(r[5])) for r in fa if r[0]]
+    cov = []
+    for b in range(len(ql)):
+        for s in range(int(ql[b])):
+            pid = b * smax + s
+            cov.append(any(lo <= pid < hi for lo, hi in wins))
+    return np.array(cov)
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(ctx=[3000, 5000, 800, 12000], q_lens=[1, 2, 1, 3], H=64, K=512, seed=41),  # plan in the attention kernel
+    dict(ctx=[3000, 900], q_lens=[400, 300], H=64, K=256, seed=42),                 # plan kernel
+], ids=["fused_plan", "plan_kernel"])
+def test_uncovered_tokens_are_zero(cfg):
+    """Metadata with a core disabled: the tokens of its window get zero output
+    and LSE, every other token is unchanged."""
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
+
+    case = U.build_case(cfg)
+    out, lse = U.run_api(case)
+    cu = np.asarray(case.cu_seqlens_q)
+    md = sparse_attn_sharedkv_metadata(
+        num_heads_q=case.H, num_heads_kv=1, head_dim=512, cu_seqlens_q=torch.tensor(cu, dtype=torch.int32),
+        seqused_kv=torch.tensor(case.seqused_kv, dtype=torch.int32), batch_size=len(cu) - 1, layout_q="TND",
+        cmp_topk=case.K, cmp_ratio=case.cmp_ratio, device="cpu").numpy().copy()
+    used = [i for i in range(36) if md[i * 8] == 1]
+    md[used[len(used) // 2] * 8] = 0  # disable a core in the middle
+    cov = _covered_tokens(md, cu)
+    assert (~cov).any() and cov.any()
+    out2, lse2 = U.run_api(case, metadata=torch.tensor(md, dtype=torch.int32, device="cuda"))
+    assert np.all(out2[~cov] == 0) and np.all(lse2[~cov] == 0)
+    assert np.array_equal(out2[cov], out[cov]) and np.array_equal(lse2[cov], lse[cov])
+
+
 def test_bsnd_layout_and_return_types():
     from dsv4_b200 import sparse_attn_sharedkv
 

@@ -436,7 +436,8 @@ def ours_arm(a, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     attn_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev2)
 
-    # e2e through the public API with pinned host inputs / outputs
+    # e2e through the public API with pinned host inputs / outputs: every step
+    # copies q and the per-step inputs host -> device and the results back
     host = {}
     for k in ("cu_seqlens_q", "seqused_kv", "ori_block_table", "cmp_block_table", "cmp_sparse_indices", "sinks"):
         if k in d:
@@ -467,6 +468,8 @@ def ours_arm(a, rank, world, local_rank):
         e1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = sum(e0.elapsed_time(e1) for e0, e1 in ev3)
+    if os.environ.get("SAS_BENCH_DEBUG"):
+        print("e2e per-step ms:", [round(e0.elapsed_time(e1), 3) for e0, e1 in ev3], file=sys.stderr)
 
     # max over ranks
     t = torch.tensor([total_ms, e2e_ms, attn_ms], dtype=torch.float64, device=dev)

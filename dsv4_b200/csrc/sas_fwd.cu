@@ -86,19 +86,18 @@ constexpr int M_CMASK = 272;     // CD x 4 words: row-validity mask per ring slo
 constexpr int M_LWORD = 384;     // 3 words: group B (loader warps) OR
 constexpr int M_SWORD = 400;     // 3 words: group A (softmax warps) OR
 constexpr int M_RANGE = 416;     // RangeInfo of this CTA (4 ints)
-constexpr int M_RED = 512;       // 4 x 64 floats = 1 KB
-constexpr int M_MRUN = 1536;     // 64 floats
-constexpr int M_ALPHA = 1792;    // 64 floats
-constexpr int M_INV = 2048;      // 64 floats
-constexpr int M_COORD = 2304;    // CD x 128 int32: pool row per chunk row (-1 = masked)
+constexpr int M_RED = 512;       // [2 chunk parities][4 quads][64 heads] per-warp maxima, 2 KB
+constexpr int M_MRUN = 2560;     // [2 groups][4 quads][32 heads] each warp's running max, 1 KB
+constexpr int M_INV = 3584;      // 64 floats: 1/l
+constexpr int M_LRED = 3840;     // [4 quads][64 heads] per-warp row sums (epilogue), 1 KB
+constexpr int M_COORD = 4864;    // CD x 128 int32: pool row per chunk row (-1 = masked)
 constexpr int M_MW = M_COORD + CD * CH * 4;  // kTmemMergeMax x 64 floats: merge weights
 constexpr int kTmemMergeMax = 4;                 // pieces merged straight from TMEM (else via L2)
 constexpr int MISC_BYTES = M_MW + kTmemMergeMax * 64 * 4;
 constexpr int kFusedMaxT = 512;  // token plans built inside the attention kernel (no plan kernel)
-// fused plan region: TokInfo[kFusedMaxT], pid[kFusedMaxT], units[kFusedMaxT + 1], smax
+// fused plan region: TokInfo[kFusedMaxT], units[kFusedMaxT + 1], smax
 constexpr int OFF_PLAN = OFF_MISC + MISC_BYTES;
-constexpr int P_PID = kFusedMaxT * 16;
-constexpr int P_US = P_PID + kFusedMaxT * 4;
+constexpr int P_US = kFusedMaxT * 16;
 constexpr int P_SMAX = P_US + (kFusedMaxT + 1) * 4;
 constexpr int PLAN_BYTES = (P_SMAX + 4 + 15) / 16 * 16;
 constexpr int SMEM_BYTES = OFF_PLAN + PLAN_BYTES + 1024;  // fused plan; + alignment slack
@@ -488,19 +487,26 @@ struct SmGroup {
   int quad, lane, gst;  // TMEM lane quadrant, lane, row = quad*32 + lane
   bool lead;
   GroupSync gs;
-  float lsum;           // running sum of head hb+lane over this warp's 32 rows
+  float lsum[32];       // running sums of heads hb..hb+31 over this thread's row
+                        // (reduced over the 128 rows once per segment)
   uint32_t lane_addr;   // TMEM address of this warp's lane quadrant
   uint32_t seg;         // segments finished
 };
 
 // Shared-memory scratch of the softmax groups (disjoint columns per group).
 struct SmShared {
-  float* red;     // [4 quads][64 heads]
-  float* m_run;   // [64] running max, log2 units
-  float* alpha;   // [64] rescale factors / merge scratch
+  float* red;     // [2 chunk parities][4 quads][64 heads] per-warp maxima
+  float* m_run;   // [2 groups][4 quads][32 heads]: each warp's own copy of the running max
   float* inv;     // [64] 1 / l
+  float* lred;    // [4 quads][64 heads] per-warp row sums of a segment
   uint8_t* pbuf;  // P^T: 128 rows x 64 heads, 128B-swizzled
+  float* scratch; // [kTmemMergeMax][64]: merge weights / LSEs
 };
+
+// This warp's running max for its group's 32 heads.
+__device__ __forceinline__ float* warp_mrun(const SmShared& S, const SmGroup& G) {
+  return S.m_run + (G.half * 4 + G.quad) * 32;
+}
 
 // The token plan this CTA uses (from the 1024-aligned shared-memory base
 // that the barriers sit in): its own fused plan, or the plan kernel's.
@@ -592,12 +598,14 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
                                               uint32_t gchunk, bool first, bool valid, int g,
                                               volatile int* abort_flag, bool tracing, unsigned long long* tr) {
   using IO = IoType<DT>;
+  float* mw = warp_mrun(S, G);  // this warp's running max, heads hb..hb+31
   if (first) {
-    if (G.gst < 32) {
-      const int h = g * HG + G.hb + G.gst;
-      S.m_run[G.hb + G.gst] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
+    {
+      const int h = g * HG + G.hb + G.lane;
+      mw[G.lane] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
     }
-    G.lsum = 0.f;
+#pragma unroll
+    for (int h = 0; h < 32; ++h) G.lsum[h] = 0.f;
   }
   if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
   sas::tc_fence_after();
@@ -619,7 +627,7 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
     w.y = sas::warp_max_f32(x[h + 1]);
     w.z = sas::warp_max_f32(x[h + 2]);
     w.w = sas::warp_max_f32(x[h + 3]);
-    if (G.lane == 0) *reinterpret_cast<float4*>(S.red + G.quad * 64 + G.hb + h) = w;
+    if (G.lane == 0) *reinterpret_cast<float4*>(S.red + (gchunk & 1) * 256 + G.quad * 64 + G.hb + h) = w;
   }
   if (tracing) {
     const long long t2 = clock64();
@@ -632,27 +640,33 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
     tr[TR_S_SYNC1] += t2 - tq;
     tq = t2;
   }
-  int need = 0;
-  if (G.gst < 32) {
-    const int c = G.hb + G.gst;
-    const float mx = fmaxf(fmaxf(S.red[c], S.red[64 + c]), fmaxf(S.red[128 + c], S.red[192 + c]));
-    const float mo = S.m_run[c];
-    float al = 1.f;
-    if (mx > mo + p.tau) {
+  // every warp merges the 4 quads' maxima itself (lane h: head hb+h) and keeps
+  // its own running max, so no second group barrier is needed; the maxima are
+  // double-buffered by chunk parity, which the group barrier of the next chunk
+  // makes safe to reuse
+  float al;
+  int need;
+  {
+    const float* rb = S.red + (gchunk & 1) * 256 + G.hb + G.lane;
+    const float mx = fmaxf(fmaxf(rb[0], rb[64]), fmaxf(rb[128], rb[192]));
+    const float mo = mw[G.lane];
+    al = 1.f;
+    const bool up = mx > mo + p.tau;
+    if (up) {
       al = sas::ex2(mo - mx);
-      S.m_run[c] = mx;
-      need = 1;
+      mw[G.lane] = mx;
     }
-    S.alpha[c] = al;
+    need = __any_sync(0xffffffffu, up);
+    __syncwarp();
   }
-  if (!G.gs.sync_or(need, G.lane, G.lead, need, abort_flag, p.status, 17)) return false;
   if (tracing) {
     const long long t2 = clock64();
     tr[TR_S_SYNC2] += t2 - tq;
     tq = t2;
   }
   if (need) {
-    G.lsum *= S.alpha[G.hb + G.lane];
+#pragma unroll
+    for (int h = 0; h < 32; ++h) G.lsum[h] *= __shfl_sync(0xffffffffu, al, h);
     if (!first) {
       // O^T holds chunks up to i-1: S^T(i) completing implies P.V(i-1) has
 #pragma unroll 1
@@ -661,7 +675,8 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
         sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
         sas::tmem_wait_ld();
 #pragma unroll
-        for (int h = 0; h < 32; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * S.alpha[G.hb + h]);
+        for (int h = 0; h < 32; ++h)
+          o[h] = __float_as_uint(__uint_as_float(o[h]) * __shfl_sync(0xffffffffu, al, h));
         sas::tmem_st32(G.lane_addr + TM_O + 64 * j + G.hb, o);
       }
       sas::tmem_wait_st();
@@ -673,7 +688,7 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
     tq = t2;
   }
 #pragma unroll
-  for (int h = 0; h < 32; ++h) x[h] = sas::ex2(x[h] - S.m_run[G.hb + h]);
+  for (int h = 0; h < 32; ++h) x[h] = sas::ex2(x[h] - mw[h]);
   uint8_t* prow = S.pbuf + G.gst * 128;
 #pragma unroll
   for (int c4 = 0; c4 < 4; ++c4) {
@@ -688,8 +703,8 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
     tr[TR_S_EXP] += t2 - tq;
     tq = t2;
   }
-  warp_reduce_scatter<32, false>(x, G.lane);
-  G.lsum += x[0];
+#pragma unroll
+  for (int h = 0; h < 32; ++h) G.lsum[h] += x[h];
   if (tracing) {
     const long long t2 = clock64();
     tr[TR_S_SUM] += t2 - tq;
@@ -720,8 +735,8 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
   const int np = r1 - r0 + 1;  // <= kTmemMergeMax
   if (G.gst < 32) {
     const int c = G.hb + G.gst, h = g * HG + c;
-    const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
-    const float own = L > 0.f ? S.m_run[c] + __log2f(L) : -INFINITY;  // as the partial's lse
+    const float L = S.lred[c] + S.lred[64 + c] + S.lred[128 + c] + S.lred[192 + c];
+    const float own = L > 0.f ? warp_mrun(S, G)[G.gst] + __log2f(L) : -INFINITY;  // as the partial's lse
     const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
     float li[kTmemMergeMax];
     float M = sink;
@@ -794,14 +809,21 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
   sas::tc_fence_after();
   const long long te0 = tracing ? clock64() : 0;
-  S.red[G.quad * 64 + G.hb + G.lane] = G.lsum;
+  {
+    // the segment's l: this warp's 32 rows, then the 4 quads through smem
+    float l[32];
+#pragma unroll
+    for (int h = 0; h < 32; ++h) l[h] = G.lsum[h];
+    warp_reduce_scatter<32, false>(l, G.lane);
+    S.lred[G.quad * 64 + G.hb + G.lane] = l[0];
+  }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 18)) return false;
 
   const size_t pslot = ((size_t)r * 2 + sg.which) * p.G + g;
   if (G.gst < 32) {
     const int c = G.hb + G.gst, h = g * HG + c;
-    const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
-    const float m = S.m_run[c];
+    const float L = S.lred[c] + S.lred[64 + c] + S.lred[128 + c] + S.lred[192 + c];
+    const float m = warp_mrun(S, G)[G.gst];  // threads 0-31 are the quad-0 warp
     if (sg.complete) {
       const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
       const float Lf = L + sas::ex2(sink - m);
@@ -859,8 +881,8 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
     } else {
     if (G.gst < 32) {
       const int c = G.hb + G.gst;
-      const float L = S.red[c] + S.red[64 + c] + S.red[128 + c] + S.red[192 + c];
-      p.part_lse[pslot * HG + c] = L > 0.f ? S.m_run[c] + __log2f(L) : -INFINITY;
+      const float L = S.lred[c] + S.lred[64 + c] + S.lred[128 + c] + S.lred[192 + c];
+      p.part_lse[pslot * HG + c] = L > 0.f ? warp_mrun(S, G)[G.gst] + __log2f(L) : -INFINITY;
     }
     float* po = p.part_o + pslot * HG * D;
 #pragma unroll 1
@@ -887,13 +909,13 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         tmem_merge = 1;
       } else {
         __threadfence();
-        if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.alpha, abort_flag)) return false;
+        if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.scratch, abort_flag)) return false;
       }
     }
     }
     if (tmem_merge) {
       __threadfence();
-      float* mw = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) - M_BAR + M_MW);
+      float* mw = S.scratch;
       if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
     }
   }
@@ -914,7 +936,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
 // those zero). The piece that merges a cut token does this after its merge,
 // so an uncovered cut token ends zero whatever the order of the pieces.
 template <int DT>
-__device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us, const int32_t* pid,
+__device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us, const TokInfo* tok,
                                const int* s_smax, const RangeInfo& ri, int g, volatile int* abort_flag) {
   using IO = IoType<DT>;
   sas::pdl_wait();  // the metadata is complete and visible
@@ -931,7 +953,8 @@ __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us
   wk.init(us, ri);
   Seg sg;
   while (wk.next(sg)) {
-    const int q = pid[sg.t];
+    const int b = tok[sg.t].b;
+    const int q = b * smax + (sg.t - (p.layout == SAS_LAYOUT_TND ? p.cu[b] : b * p.S));  // pid of kernel.py
     int covered;
     if (!G.gs.sync_or(q >= lin0 && q < lin1, G.lane, G.lead, covered, abort_flag, p.status, 24)) return false;
     if (covered) continue;
@@ -953,8 +976,7 @@ __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us
 // metadata and it can run while the metadata kernel is still in flight.
 // Output rows of tokens without work are zeroed, each by one CTA.
 template <int DT>
-__device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_pid, int32_t* s_us, int* s_smax,
-                           int* s_wsum) {
+__device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, int* s_smax, int* s_wsum) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kW = kThreads / 32;
   // max_seq: the reference api's S_max (api.py:208-215 / 229)
@@ -983,7 +1005,6 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_pid, i
       units = p.n_win_chunks + (n_cmp + CH - 1) / CH;
     }
     s_tok[t] = ti;
-    s_pid[t] = b * smax + s;
     s_us[t] = units;
   };
   if (p.layout == SAS_LAYOUT_TND) {
@@ -1054,14 +1075,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   int32_t* coords = reinterpret_cast<int32_t*>(misc + M_COORD);          // [CD][128]
   float* red = reinterpret_cast<float*>(misc + M_RED);
   float* m_run = reinterpret_cast<float*>(misc + M_MRUN);
-  float* alpha_s = reinterpret_cast<float*>(misc + M_ALPHA);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
   // the token plan: this CTA's own (FUSED) or the plan kernel's
   TokInfo* s_tok = reinterpret_cast<TokInfo*>(smem + OFF_PLAN);
   int32_t* s_us = reinterpret_cast<int32_t*>(smem + OFF_PLAN + P_US);
   const int32_t* usp = FUSED ? s_us : p.unit_start;
   const TokInfo* tokp = FUSED ? s_tok : p.tok;
-  const SmShared sm{red, m_run, alpha_s, inv_s, smem + OFF_P};
+  const SmShared sm{red, m_run, inv_s, reinterpret_cast<float*>(misc + M_LRED), smem + OFF_P,
+                    reinterpret_cast<float*>(misc + M_MW)};
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
@@ -1105,7 +1126,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the metadata is only waited for when a token's output is written
   if (!p.early) sas::pdl_wait();
   if constexpr (FUSED)
-    fused_plan<DT>(p, s_tok, reinterpret_cast<int32_t*>(smem + OFF_PLAN + P_PID), s_us,
+    fused_plan<DT>(p, s_tok, s_us,
                    reinterpret_cast<int*>(smem + OFF_PLAN + P_SMAX), reinterpret_cast<int*>(red));
   if (warp == 0) {
     const RangeInfo ri = compute_range(usp, p.T, p.R, r, lane);
@@ -1227,7 +1248,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = lane >> 3, c16 = lane & 7;
     const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
     SmGroup G{32, 1, lw, lane, lw * 32 + lane, lw == 0,
-              GroupSync{&bars[B_LSYNC], reinterpret_cast<uint32_t*>(misc + M_LWORD), 0}, 0.f,
+              GroupSync{&bars[B_LSYNC], reinterpret_cast<uint32_t*>(misc + M_LWORD), 0}, {},
               tmem + ((uint32_t)(lw * 32) << 16), 0};
     unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
@@ -1299,7 +1320,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok && have_pend) ok = segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb);
     if (FUSED && ok)
-      zero_uncovered<DT>(p, G, usp, reinterpret_cast<const int32_t*>(smem + OFF_PLAN + P_PID),
+      zero_uncovered<DT>(p, G, usp, tokp,
                          reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   } else if (warp == kMmaWarp) {
@@ -1383,7 +1404,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =============================== softmax group A (heads 0-31) / epilogue
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
     SmGroup G{0, 0, quad, lane, quad * 32 + lane, quad == 0,
-              GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, 0.f,
+              GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, {},
               tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
     wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
@@ -1412,7 +1433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     if (FUSED && ok)
-      zero_uncovered<DT>(p, G, usp, reinterpret_cast<const int32_t*>(smem + OFF_PLAN + P_PID),
+      zero_uncovered<DT>(p, G, usp, tokp,
                          reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   }

@@ -17,6 +17,10 @@ Workloads (synthetic N(0,1) data, seeded):
   C5: long-context decode, 512 requests length-balanced over the N GPUs
       (strong scaling), 128 heads, K=1024, contexts U[64k, 256k].
 
+--mode heads (with any config): the head-sharded variant. Every rank holds
+every request and computes H/N heads; the outputs and LSEs are all-gathered
+with NCCL (dsv4_b200/sharding.py). Strong scaling; KV is read by every GPU.
+
 The JSON line carries: value (query tokens/s, whole job), ms_per_step,
 roofline of the dominant kernel (the attention kernel alone, timed live with
 CUDA events; algorithmic bytes = unique KV rows x 1 KB + Q + out + LSE +
@@ -55,6 +59,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="C2", choices=["C1", "C2", "C3", "C4", "C5"])
+    ap.add_argument("--mode", default="requests", choices=["requests", "heads"],
+                    help="requests: each rank runs its own requests (no collective); heads: every rank runs "
+                         "H/N heads of all requests and the outputs are all-gathered over NCCL")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -64,10 +71,14 @@ def parse():
     return a
 
 
-def workload(cfg: str, rank: int, world: int):
-    """(ctx list, q_lens list, H, K, block size, description) for this rank."""
+def workload(cfg: str, rank: int, world: int, mode: str = "requests"):
+    """(ctx list, q_lens list, H, K, block size, scaling) for this rank."""
     from dsv4_b200 import synth
 
+    if mode == "heads":
+        # every rank holds every request (same seed) and computes H/world heads
+        c = synth.config_contexts(cfg, seed=0)
+        return c["ctx"], c["q_lens"], c["H"], c["K"], c["bs"], "strong"
     if cfg == "C5":
         c = synth.config_contexts("C5", seed=0)
         part = synth.balance_requests(c["ctx"], world)[rank]
@@ -348,8 +359,9 @@ def ours_arm(a, rank, world, local_rank):
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    ctx, ql, H, K, bs, scaling = workload(a.config, rank, world)
-    d = synth.make_case_torch(ctx=ctx, q_lens=ql, H=H, K=K, bs=bs, seed=1000 + rank, device=dev)
+    ctx, ql, H, K, bs, scaling = workload(a.config, rank, world, a.mode)
+    heads = a.mode == "heads"
+    d = synth.make_case_torch(ctx=ctx, q_lens=ql, H=H, K=K, bs=bs, seed=1000 if heads else 1000 + rank, device=dev)
     q = d.pop("q")
     d.pop("topk_cmp", None)
     T = q.shape[0]
@@ -358,8 +370,17 @@ def ours_arm(a, rank, world, local_rank):
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    def step():
-        sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, **d)
+    from dsv4_b200.sharding import head_sharded_forward, head_range
+
+    h0, h1 = head_range(H, world, rank) if heads else (0, H)
+    if heads and world > 1:
+        def step():
+            o, l = head_sharded_forward(q, **dict(d))
+            out.copy_(o)
+            lse.copy_(l)
+    else:
+        def step():
+            sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, **d)
 
     # correctness gate before timing (status word + finite output)
     step()
@@ -368,7 +389,7 @@ def ours_arm(a, rank, world, local_rank):
     assert torch.isfinite(out.float()).all()
 
     graph = None
-    if not a.no_graph:
+    if not a.no_graph and not heads:  # the head-sharded step (NCCL all-gather) runs eagerly
         s = torch.cuda.Stream(dev)
         s.wait_stream(stream)
         with torch.cuda.stream(s):
@@ -421,17 +442,25 @@ def ours_arm(a, rank, world, local_rank):
 
     # attention kernel alone (the dominant kernel), same stream, flushed L2:
     # metadata and plan computed once, then only the attention launch is timed
+    # (head-sharded mode: this rank's H/N heads)
+    qa, da, Ha = q, d, H
+    if heads:
+        qa = q[:, h0:h1].contiguous()
+        da = dict(d, sinks=d["sinks"][h0:h1].contiguous())
+        Ha = h1 - h0
+    outa = torch.empty_like(qa)
+    lsea = torch.empty((T, Ha), dtype=torch.float32, device=dev)
     md = sparse_attn_sharedkv_metadata(
-        num_heads_q=H, num_heads_kv=1, head_dim=512, cu_seqlens_q=d["cu_seqlens_q"], seqused_kv=d["seqused_kv"],
+        num_heads_q=Ha, num_heads_kv=1, head_dim=512, cu_seqlens_q=d["cu_seqlens_q"], seqused_kv=d["seqused_kv"],
         batch_size=len(ctx), layout_q="TND", cmp_topk=K, cmp_ratio=4, device=dev)
-    sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, metadata=md, _stages=_lib.STAGE_PLAN,
-                         **d)
+    sparse_attn_sharedkv(qa, out=outa, lse_out=lsea, return_softmax_lse=True, metadata=md,
+                         _stages=_lib.STAGE_PLAN, **da)
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
     for e0, e1 in ev2:
         flush.zero_()
         e0.record(stream)
-        sparse_attn_sharedkv(q, out=out, lse_out=lse, return_softmax_lse=True, metadata=md,
-                             _stages=_lib.STAGE_ATTENTION, **d)
+        sparse_attn_sharedkv(qa, out=outa, lse_out=lsea, return_softmax_lse=True, metadata=md,
+                             _stages=_lib.STAGE_ATTENTION, **da)
         e1.record(stream)
     torch.cuda.synchronize(dev)
     attn_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev2)
@@ -453,7 +482,10 @@ def ours_arm(a, rank, world, local_rank):
         qd = hq.to(dev, non_blocking=True)
         for k, v in host.items():
             dd[k] = v.to(dev, non_blocking=True)
-        o, l = sparse_attn_sharedkv(qd, return_softmax_lse=True, **dd)
+        if heads and world > 1:
+            o, l = head_sharded_forward(qd, **dict(dd))
+        else:
+            o, l = sparse_attn_sharedkv(qd, return_softmax_lse=True, **dd)
         hout.copy_(o, non_blocking=True)
         hlse.copy_(l, non_blocking=True)
 
@@ -477,14 +509,14 @@ def ours_arm(a, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ntok = torch.tensor([T], dtype=torch.float64, device=dev)
         dist.all_reduce(ntok)
-        tokens_all = int(ntok.item())
+        tokens_all = T if heads else int(ntok.item())
     else:
         tokens_all = T
     total_ms, e2e_ms, attn_ms_max = t.tolist()
 
     if rank != 0:
         return
-    work = algorithmic_work(dict(d, q=q), H, K)
+    work = algorithmic_work(dict(d, q=qa), Ha, K)
     peaks = {}
     pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pk):
@@ -507,7 +539,8 @@ def ours_arm(a, rank, world, local_rank):
         "config": {"workload": a.config + ": " + describe(a.config, world), "tokens_per_gpu": T, "heads": H,
                    "topk": K, "head_dim": 512, "window": 128, "cmp_ratio": 4, "block": bs,
                    "l2": "flushed (512 MB write) between timed steps", "graph": graph is not None,
-                   "parallelism": f"request-parallel x{world}"},
+                   "parallelism": (f"head-sharded x{world} ({H // world} heads/GPU, NCCL all-gather)" if heads
+                                   else f"request-parallel x{world}")},
         "us_per_layer": total_ms / a.steps * 1e3,
         "attention_kernel_us": attn_ms * 1e3,
         "hbm_gbs_attention": achieved,

@@ -176,7 +176,7 @@ enum TraceSlot {
   TR_TOTAL = 0, TR_P_COORD, TR_P_WAIT_EMPTY, TR_P_WAIT_MASK, TR_P_ISSUE, TR_M_WAIT_Q, TR_M_WAIT_FULL,
   TR_M_WAIT_P, TR_M_WAIT_O, TR_S_WAIT_MASK, TR_S_WAIT_S, TR_S_SOFTMAX, TR_S_WAIT_O, TR_S_EPI, TR_CHUNKS,
   TR_SEGS, TR_E_TMEM, TR_E_STAGE, TR_E_COPY, TR_E_RED, TR_S_LD, TR_S_SYNC1, TR_S_SYNC2, TR_S_EXP,
-  TR_S_SUM, TR_S_FENCE, TR_S_RESCALE, TR_S_MAX, TR_NSLOTS = 28
+  TR_S_SUM, TR_S_FENCE, TR_S_RESCALE, TR_S_MAX, TR_FIRST_S, TR_PROLOGUE, TR_NSLOTS = 30
 };
 
 __device__ __forceinline__ int py_floordiv(int a, int b) {
@@ -610,6 +610,7 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
   if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
   sas::tc_fence_after();
   const long long ts0 = tracing ? clock64() : 0;
+  if (tracing && tr[TR_FIRST_S] == 0) tr[TR_FIRST_S] = ts0;  // absolute; made relative at the end
   float x[32];
   {
     uint32_t ra[32];
@@ -982,7 +983,14 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
   // max_seq: the reference api's S_max (api.py:208-215 / 229)
   int mx = 0;
   if (p.layout == SAS_LAYOUT_TND) {
-    for (int b = tid; b < p.B; b += kThreads) mx = max(mx, p.cu[b + 1] - p.cu[b]);
+    // seqused_kv is loaded in this first pass too (into L1), so the per-request
+    // pass below finds both arrays there: one cold round trip, not two
+    int kv = 0;
+    for (int b = tid; b < p.B; b += kThreads) {
+      mx = max(mx, p.cu[b + 1] - p.cu[b]);
+      kv |= p.seqused_kv[b];
+    }
+    if (kv == -1) mx = max(mx, 0);  // keeps the loads; never true for valid lengths
   } else {
     mx = p.S;
   }
@@ -1065,6 +1073,7 @@ template <int DT, bool TRACE, bool FUSED>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const long long t_entry = TRACE ? clock64() : 0;
   const uint32_t raw_addr = sas::smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
   uint8_t* misc = smem + OFF_MISC;
@@ -1461,10 +1470,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tp[TR_CHUNKS] = tr[TR_CHUNKS];
       tp[TR_SEGS] = tr[TR_SEGS];
       tp[TR_TOTAL] = clock64() - t_start;
+      tp[TR_FIRST_S] = tr[TR_FIRST_S] ? tr[TR_FIRST_S] - t_start : 0;
+      tp[TR_PROLOGUE] = t_start - t_entry;
       tp[TR_E_TMEM] = tr[TR_E_TMEM];
       tp[TR_E_STAGE] = tr[TR_E_STAGE];
       tp[TR_E_RED] = tr[TR_E_RED];
-      for (int i = TR_S_LD; i < TR_NSLOTS; ++i) tp[i] = tr[i];
+      for (int i = TR_S_LD; i < TR_FIRST_S; ++i) tp[i] = tr[i];
     }
   }
   sas::tc_fence_before();

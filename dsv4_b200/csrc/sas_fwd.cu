@@ -59,33 +59,47 @@ constexpr int CH = 128;       // KV rows per chunk (MMA M)
 constexpr int NSLAB = 8;      // 64-column slabs per chunk
 constexpr int SLAB_BYTES = CH * 128;  // 16 KB
 constexpr int Q_SLAB_BYTES = HG * 128;  // 8 KB
-constexpr int kLoaderWarps = 4;         // warps 0-3: cp.async loaders
+// 12 warps, 3 per SM sub-partition (so 168 registers per thread):
+constexpr int kLoaderWarps = 2;         // warps 0-1: cp.async copies of K and V rows
 constexpr int kLoaderThreads = 32 * kLoaderWarps;
-constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax / epilogue
-constexpr int kMmaWarp = 8;             // warp 8: TMEM owner and MMA issuer
-constexpr int kCoordWarp = 9;           // warp 9: row resolution + L2 prefetch, runs ahead
-constexpr int kThreads = 32 * 10;
+constexpr int kMmaWarp = 2;             // warp 2: TMEM owner and MMA issuer
+constexpr int kCoordWarp = 3;           // warp 3: row resolution + L2 prefetch, runs ahead
+constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax group A (heads 0-31) / epilogue
+constexpr int kSoftmaxWarpB = 8;        // warps 8-11: softmax group B (heads 32-63) / epilogue
+constexpr int kThreads = 32 * 12;
 constexpr int CD = 4;                    // depth of the row-coordinate ring (chunks)
 // Chunks a token may hold beyond a range's length before it is cut across
 // ranges: a cut costs the partial write-back and the merge, about this many
 // chunks of work.
-constexpr int kCutCost = 3;
+constexpr int kCutCost = 1;  // in units (tiles)
+// A unit of work is one softmax tile of a token, as golden.py tiles the KV
+// (GOLDEN_S2_TILE = 512 rows): the window rows, then the compressed rows in
+// tiles of 512, i.e. up to kTileChunks 128-row chunks. The running max is
+// updated once per tile with the tile's exact max, so P is rounded at the
+// same points as the reference.
+constexpr int kTileChunks = 4;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 // shared memory map (offsets from a 1024-aligned base)
+// The K/V ring holds kRing 16 KB slabs. A chunk is 8 slabs; slab number n
+// (counted over every chunk copy) lives in slot n % kRing. kRing is even and
+// every chunk starts on an even slab number, so the slab pair (2j, 2j+1) of
+// P.V's d-tile j always sits in two adjacent slots (fixed operand stride).
+constexpr int kRing = 6;
+constexpr int P_BYTES = CH * 128;                         // one P^T buffer, 16 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = OFF_Q + NSLAB * Q_SLAB_BYTES;     // 64 KB
-constexpr int OFF_P = OFF_KV + NSLAB * SLAB_BYTES;       // +128 KB
-constexpr int OFF_MISC = OFF_P + CH * 128;               // +16 KB
+constexpr int OFF_P = OFF_KV + kRing * SLAB_BYTES;       // +96 KB
+constexpr int OFF_MISC = OFF_P + 2 * P_BYTES;            // +32 KB (double-buffered P^T)
 // misc region
-constexpr int M_BAR = 0;         // 32 mbarriers x 8 B
-constexpr int M_TMEM = 256;      // tmem base address
-constexpr int M_ABORT = 260;
-constexpr int M_CMASK = 272;     // CD x 4 words: row-validity mask per ring slot
-constexpr int M_LWORD = 384;     // 3 words: group B (loader warps) OR
-constexpr int M_SWORD = 400;     // 3 words: group A (softmax warps) OR
-constexpr int M_RANGE = 416;     // RangeInfo of this CTA (4 ints)
+constexpr int M_BAR = 0;         // 40 mbarriers x 8 B
+constexpr int M_TMEM = 320;      // tmem base address
+constexpr int M_ABORT = 324;
+constexpr int M_CMASK = 336;     // CD x 4 words: row-validity mask per ring slot
+constexpr int M_LWORD = 400;     // 3 words: group B (loader warps) OR
+constexpr int M_SWORD = 416;     // 3 words: group A (softmax warps) OR
+constexpr int M_RANGE = 432;     // RangeInfo of this CTA (4 ints)
 constexpr int M_RED = 512;       // [2 chunk parities][4 quads][64 heads] per-warp maxima, 2 KB
 constexpr int M_MRUN = 2560;     // [2 groups][4 quads][32 heads] each warp's running max, 1 KB
 constexpr int M_INV = 3584;      // 64 floats: 1/l
@@ -105,22 +119,25 @@ constexpr int SMEM_BYTES_BASE = OFF_PLAN + 1024;           // plan kernel's plan
 static_assert(SMEM_BYTES <= 232448, "shared memory over the per-CTA limit");
 
 // barrier indices
-constexpr int B_FULL = 0;        // 8
-constexpr int B_EMPTY = 8;       // 8
+constexpr int B_FULL = 0;        // kRing
+constexpr int B_EMPTY = 8;       // kRing
 constexpr int B_QFULL = 16;
 constexpr int B_QEMPTY = 17;
 constexpr int B_SFULL = 18;
-constexpr int B_PREADY = 19;
 constexpr int B_OFULL = 20;
 constexpr int B_OEMPTY = 21;
+// Per P^T buffer b (chunk n uses buffer n % 2), so that each completes once per
+// two chunks and no waiter can fall two phases behind:
+constexpr int B_PREADY2 = 32;    // 2: P^T(n) written by both softmax groups (256 arrivals)
+constexpr int B_PFREE = 34;      // 2: P.V(n) done, buffer n % 2 may be rewritten
 constexpr int B_CFULL = 22;      // CD: coordinate ring slot written
 constexpr int B_LSYNC = 26;      // group barrier of softmax group B (warps 0-3)
 constexpr int B_SSYNC = 27;      // group barrier of softmax group A (warps 4-7)
 constexpr int B_CEMPTY = 28;     // CD: slot read by the 4 loader and 4 softmax warps
 
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TM_S = 0;
-constexpr uint32_t TM_O = 64;
+constexpr uint32_t TM_S = 0;     // S^T of the tile's chunks: kTileChunks slots of 64 columns
+constexpr uint32_t TM_O = 256;   // O^T: 4 d-tiles of 64 columns
 
 struct TokInfo {
   int b, s_g, n_cmp, thr;
@@ -178,6 +195,25 @@ enum TraceSlot {
   TR_SEGS, TR_E_TMEM, TR_E_STAGE, TR_E_COPY, TR_E_RED, TR_S_LD, TR_S_SYNC1, TR_S_SYNC2, TR_S_EXP,
   TR_S_SUM, TR_S_FENCE, TR_S_RESCALE, TR_S_MAX, TR_FIRST_S, TR_PROLOGUE, TR_NSLOTS = 30
 };
+
+// Tiles of a token: ceil(window chunks / 4) window tiles, then the
+// compressed chunks in groups of 4 (golden.py walks ori tiles, then cmp tiles).
+__device__ __forceinline__ int token_tiles(int n_win_chunks, int n_cmp) {
+  return (n_win_chunks + kTileChunks - 1) / kTileChunks + ((n_cmp + CH - 1) / CH + kTileChunks - 1) / kTileChunks;
+}
+// Chunk range [c0, c1) of tile k (chunk c < n_win_chunks is a window chunk,
+// else compressed chunk c - n_win_chunks).
+__device__ __forceinline__ void tile_chunks(int k, int n_win_chunks, int n_cmp, int& c0, int& c1) {
+  const int nwt = (n_win_chunks + kTileChunks - 1) / kTileChunks;
+  if (k < nwt) {
+    c0 = k * kTileChunks;
+    c1 = min(c0 + kTileChunks, n_win_chunks);
+  } else {
+    const int ncc = (n_cmp + CH - 1) / CH;
+    c0 = n_win_chunks + (k - nwt) * kTileChunks;
+    c1 = n_win_chunks + min((k - nwt + 1) * kTileChunks, ncc);
+  }
+}
 
 __device__ __forceinline__ int py_floordiv(int a, int b) {
   int q = a / b, r = a % b;
@@ -256,7 +292,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
         ti.s_g = s_g;
         ti.n_cmp = n_cmp;
         ti.thr = thr;
-        if (covered) units = p.n_win_chunks + (n_cmp + CH - 1) / CH;
+        if (covered) units = token_tiles(p.n_win_chunks, n_cmp);
       }
       p.tok[t] = ti;
       if (units == 0) {
@@ -589,87 +625,105 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
   return true;
 }
 
-// Softmax of one chunk for the group's 32 heads: scores from S^T, per-head
-// max over the chunk's 128 rows (warp redux + 4-way smem merge), lazy O^T
-// rescale when a running max grows by more than tau, p = 2^(x - m) written to
-// P^T rounded to the I/O dtype, l += sum of the unrounded p.
+// Max pass over one tile for the group's 32 heads (golden.py:187-190): the
+// per-head max of the tile's scores (masked rows excluded) over the 128 rows
+// of every chunk, merged over the 4 quads; the running max m becomes
+// max(m, tile max). Every warp merges the quads' maxima itself and keeps its
+// own copy of m, so one group barrier suffices; the maxima are double-buffered
+// by tile parity. al / need: the rescale factor 2^(m_old - m_new) of this
+// thread's lane head, and whether any head's max moved.
 template <int DT>
-__device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
-                                              uint32_t gchunk, bool first, bool valid, int g,
+__device__ __forceinline__ bool tile_max_pass(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
+                                              const uint32_t* cmask, uint32_t gtile, uint32_t gch0, int nch,
+                                              bool first_tile_of_seg, int g, float& al, int& need,
                                               volatile int* abort_flag, bool tracing, unsigned long long* tr) {
-  using IO = IoType<DT>;
-  float* mw = warp_mrun(S, G);  // this warp's running max, heads hb..hb+31
-  if (first) {
-    {
-      const int h = g * HG + G.hb + G.lane;
-      mw[G.lane] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
-    }
+  float* mw = warp_mrun(S, G);
+  if (first_tile_of_seg) {
+    const int h = g * HG + G.hb + G.lane;
+    mw[G.lane] = h < p.H ? p.sinks[h] * kLog2e : 0.f;  // (m, l) start at (sink, 1): golden.py:162-163
 #pragma unroll
-    for (int h = 0; h < 32; ++h) G.lsum[h] = 0.f;
+    for (int h2 = 0; h2 < 32; ++h2) G.lsum[h2] = 0.f;
   }
-  if (!twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
+  if (!twait(&bars[B_SFULL], gtile & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
   sas::tc_fence_after();
   const long long ts0 = tracing ? clock64() : 0;
-  if (tracing && tr[TR_FIRST_S] == 0) tr[TR_FIRST_S] = ts0;  // absolute; made relative at the end
-  float x[32];
-  {
-    uint32_t ra[32];
-    sas::tmem_ld32(G.lane_addr + TM_S + G.hb, ra);
-    sas::tmem_wait_ld();
+  float mx[32];
 #pragma unroll
-    for (int h = 0; h < 32; ++h) x[h] = valid ? __uint_as_float(ra[h]) * p.scale_log2 : -INFINITY;
+  for (int h = 0; h < 32; ++h) mx[h] = -INFINITY;
+#pragma unroll 1
+  for (int i = 0; i < nch; ++i) {
+    const bool valid = (cmask[((gch0 + i) % CD) * 4 + G.quad] >> G.lane) & 1;
+    uint32_t ra[32];
+    sas::tmem_ld32(G.lane_addr + TM_S + 64 * i + G.hb, ra);
+    sas::tmem_wait_ld();
+    if (valid) {
+#pragma unroll
+      for (int h = 0; h < 32; ++h) mx[h] = fmaxf(mx[h], __uint_as_float(ra[h]) * p.scale_log2);
+    }
   }
-  long long tq = tracing ? clock64() : 0;
-  if (tracing) tr[TR_S_LD] += tq - ts0;
 #pragma unroll
   for (int h = 0; h < 32; h += 4) {
     float4 w;
-    w.x = sas::warp_max_f32(x[h]);
-    w.y = sas::warp_max_f32(x[h + 1]);
-    w.z = sas::warp_max_f32(x[h + 2]);
-    w.w = sas::warp_max_f32(x[h + 3]);
-    if (G.lane == 0) *reinterpret_cast<float4*>(S.red + (gchunk & 1) * 256 + G.quad * 64 + G.hb + h) = w;
-  }
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_MAX] += t2 - tq;
-    tq = t2;
+    w.x = sas::warp_max_f32(mx[h]);
+    w.y = sas::warp_max_f32(mx[h + 1]);
+    w.z = sas::warp_max_f32(mx[h + 2]);
+    w.w = sas::warp_max_f32(mx[h + 3]);
+    if (G.lane == 0) *reinterpret_cast<float4*>(S.red + (gtile & 1) * 256 + G.quad * 64 + G.hb + h) = w;
   }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 16)) return false;
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_SYNC1] += t2 - tq;
-    tq = t2;
-  }
-  // every warp merges the 4 quads' maxima itself (lane h: head hb+h) and keeps
-  // its own running max, so no second group barrier is needed; the maxima are
-  // double-buffered by chunk parity, which the group barrier of the next chunk
-  // makes safe to reuse
-  float al;
-  int need;
   {
-    const float* rb = S.red + (gchunk & 1) * 256 + G.hb + G.lane;
-    const float mx = fmaxf(fmaxf(rb[0], rb[64]), fmaxf(rb[128], rb[192]));
+    const float* rb = S.red + (gtile & 1) * 256 + G.hb + G.lane;
+    const float tmx = fmaxf(fmaxf(rb[0], rb[64]), fmaxf(rb[128], rb[192]));
     const float mo = mw[G.lane];
+    const bool up = tmx > mo + p.tau;
     al = 1.f;
-    const bool up = mx > mo + p.tau;
     if (up) {
-      al = sas::ex2(mo - mx);
-      mw[G.lane] = mx;
+      al = sas::ex2(mo - tmx);
+      mw[G.lane] = tmx;
     }
     need = __any_sync(0xffffffffu, up);
     __syncwarp();
   }
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_SYNC2] += t2 - tq;
-    tq = t2;
+  if (tracing) tr[TR_S_MAX] += clock64() - ts0;
+  return true;
+}
+
+// Exp pass of one chunk of the tile: p = 2^(x - m) with the tile's m (masked
+// rows give 0), rounded to the I/O dtype into P^T, l += sum of the unrounded
+// p (golden.py:191-195). The first chunk of a tile applies the tile's rescale
+// to l and O^T (golden.py:192,196) once the previous P.V is done.
+template <int DT>
+__device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
+                                               const uint32_t* cmask, uint32_t gchunk, int i, bool rescale_now,
+                                               bool first_tile_of_seg, float al, uint32_t& gp,
+                                               volatile int* abort_flag, bool tracing, unsigned long long* tr) {
+  using IO = IoType<DT>;
+  const long long ts0 = tracing ? clock64() : 0;
+  const float* mw = warp_mrun(S, G);
+  const bool valid = (cmask[(gchunk % CD) * 4 + G.quad] >> G.lane) & 1;
+  float x[32];
+  {
+    uint32_t ra[32];
+    sas::tmem_ld32(G.lane_addr + TM_S + 64 * i + G.hb, ra);
+    sas::tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < 32; ++h) x[h] = valid ? sas::ex2(__uint_as_float(ra[h]) * p.scale_log2 - mw[h]) : 0.f;
   }
-  if (need) {
+  // P buffer gp % 2 is free once P.V of chunk gp - 2 is done (phase
+  // (gp - 2) / 2 of that buffer's barrier); a rescale of O^T also needs
+  // P.V of chunk gp - 1 done
+  if (gp > 1 && !twait(&bars[B_PFREE + (gp & 1)], ((gp - 2) >> 1) & 1, abort_flag, p.status, 13, tracing,
+                       tr[TR_S_WAIT_O]))
+    return false;
+  if (rescale_now && gp > 0 &&
+      !twait(&bars[B_PFREE + ((gp - 1) & 1)], ((gp - 1) >> 1) & 1, abort_flag, p.status, 13, tracing,
+             tr[TR_S_WAIT_O]))
+    return false;
+  sas::tc_fence_after();
+  if (rescale_now) {
 #pragma unroll
     for (int h = 0; h < 32; ++h) G.lsum[h] *= __shfl_sync(0xffffffffu, al, h);
-    if (!first) {
-      // O^T holds chunks up to i-1: S^T(i) completing implies P.V(i-1) has
+    if (!first_tile_of_seg) {
 #pragma unroll 1
       for (int j = 0; j < 4; ++j) {
         uint32_t o[32];
@@ -683,14 +737,9 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
       sas::tmem_wait_st();
     }
   }
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_RESCALE] += t2 - tq;
-    tq = t2;
-  }
 #pragma unroll
-  for (int h = 0; h < 32; ++h) x[h] = sas::ex2(x[h] - mw[h]);
-  uint8_t* prow = S.pbuf + G.gst * 128;
+  for (int h = 0; h < 32; ++h) G.lsum[h] += x[h];
+  uint8_t* prow = S.pbuf + (gp & 1) * P_BYTES + G.gst * 128;
 #pragma unroll
   for (int c4 = 0; c4 < 4; ++c4) {
     const int cc = (G.hb >> 3) + c4;  // 16-byte column chunk of the 128-byte row
@@ -699,22 +748,10 @@ __device__ __forceinline__ bool softmax_chunk(const FwdParams& p, SmGroup& G, co
         make_uint4(IO::pack(x[h], x[h + 1]), IO::pack(x[h + 2], x[h + 3]), IO::pack(x[h + 4], x[h + 5]),
                    IO::pack(x[h + 6], x[h + 7]));
   }
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_EXP] += t2 - tq;
-    tq = t2;
-  }
-#pragma unroll
-  for (int h = 0; h < 32; ++h) G.lsum[h] += x[h];
-  if (tracing) {
-    const long long t2 = clock64();
-    tr[TR_S_SUM] += t2 - tq;
-    tq = t2;
-  }
   sas::fence_proxy_async_smem();
   sas::tc_fence_before();
-  sas::mbar_arrive(&bars[B_PREADY]);
-  if (tracing) tr[TR_S_FENCE] += clock64() - tq;
+  sas::mbar_arrive(&bars[B_PREADY2 + (gp & 1)]);
+  ++gp;
   if (tracing) {
     tr[TR_S_SOFTMAX] += clock64() - ts0;
     tr[TR_CHUNKS] += 1;
@@ -1010,7 +1047,7 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
       ti.s_g = s_g;
       ti.n_cmp = n_cmp;
       ti.thr = thr;
-      units = p.n_win_chunks + (n_cmp + CH - 1) / CH;
+      units = token_tiles(p.n_win_chunks, n_cmp);
     }
     s_tok[t] = ti;
     s_us[t] = units;
@@ -1097,19 +1134,22 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int r = blockIdx.x / p.G, g = blockIdx.x % p.G;
 
   if (tid == 0) {
-    for (int i = 0; i < NSLAB; ++i) {
+    for (int i = 0; i < kRing; ++i) {
       sas::mbar_init(&bars[B_FULL + i], kLoaderThreads);
       sas::mbar_init(&bars[B_EMPTY + i], 1);
     }
     sas::mbar_init(&bars[B_QFULL], 1);
     sas::mbar_init(&bars[B_QEMPTY], 1);
     sas::mbar_init(&bars[B_SFULL], 1);
-    sas::mbar_init(&bars[B_PREADY], 256);
     sas::mbar_init(&bars[B_OFULL], 1);
     sas::mbar_init(&bars[B_OEMPTY], 256);
+    for (int i = 0; i < 2; ++i) {
+      sas::mbar_init(&bars[B_PREADY2 + i], 256);
+      sas::mbar_init(&bars[B_PFREE + i], 1);
+    }
     for (int i = 0; i < CD; ++i) {
       sas::mbar_init(&bars[B_CFULL + i], 1);
-      sas::mbar_init(&bars[B_CEMPTY + i], 8);
+      sas::mbar_init(&bars[B_CEMPTY + i], kLoaderWarps + 8);
     }
     sas::mbar_init(&bars[B_SSYNC], 4);
     sas::mbar_init(&bars[B_LSYNC], 4);
@@ -1165,10 +1205,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     while (ok && wk.next(sg)) {
       const TokInfo ti = tokp[sg.t];
+      int cb_c, ce_c, dummy;  // the segment's chunk range
+      tile_chunks(sg.cb, p.n_win_chunks, ti.n_cmp, cb_c, dummy);
+      tile_chunks(sg.ce - 1, p.n_win_chunks, ti.n_cmp, dummy, ce_c);
       // the compressed scan stops at the first -1 (golden.py:55-56): a range
       // that starts inside a token looks for one in the slots before it
       bool stopped = false;
-      const int cmp_c0 = max(sg.cb - p.n_win_chunks, 0);
+      const int cmp_c0 = max(cb_c - p.n_win_chunks, 0);
       if (p.scenario == 3 && cmp_c0 > 0) {
         const int lim = min(cmp_c0 * CH, ti.n_cmp);
         const int32_t* ip = p.idx + (size_t)sg.t * p.K;
@@ -1176,7 +1219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
         stopped = __any_sync(0xffffffffu, neg);
       }
-      for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
+      for (int c = cb_c; c < ce_c; ++c, ++gchunk) {
         const long long tc0 = tracing ? clock64() : 0;
         const bool is_win = c < p.n_win_chunks;
         const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
@@ -1248,25 +1291,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp < kLoaderWarps) {
-    // =============================== loaders (+ softmax group B, heads 32-63)
-    // Per chunk: copy the resolved rows, then do the softmax of the same chunk
-    // for heads 32-63 while its S^T is ready and before the next copies can
-    // start (they wait for this chunk's P.V). A segment's epilogue runs after
-    // the next segment's first copies have been issued.
-    const int lw = warp;                // rows [32*lw, 32*lw+32) of every chunk
+    // =============================== loaders: K rows, then V rows, per tile
+    // The copies run in the MMA's consumption order (K of every chunk of a
+    // tile, then V of every chunk) and block only on ring slots, which QK^T
+    // and P.V free as they read them.
+    const int lw = warp;  // rows [64*lw, 64*lw+64) of every chunk
     const int sub = lane >> 3, c16 = lane & 7;
     const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
-    SmGroup G{32, 1, lw, lane, lw * 32 + lane, lw == 0,
-              GroupSync{&bars[B_LSYNC], reinterpret_cast<uint32_t*>(misc + M_LWORD), 0}, {},
-              tmem + ((uint32_t)(lw * 32) << 16), 0};
-    unsigned long long trb[TR_NSLOTS];  // group B's softmax timings are not reported
     Walker wk;
     wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
-    Seg sg, pend;
-    bool have_pend = false;
-    uint32_t gchunk = 0, seg_i = 0;
+    Seg sg;
+    uint32_t sc = 0, gchunk = 0, seg_i = 0;  // sc: ring slabs filled so far
     const uint32_t q_bytes = (uint32_t)NSLAB * p.q_box_h * 128;
     bool ok = true;
+    // copy the 128 rows of chunk-slot `cslot` (pool rows resolved by the
+    // coordinate warp) into the ring: one 16 KB slab per mbarrier
+    auto load_chunk = [&](uint32_t cslot, bool is_win) -> bool {
+      int crw[16];  // rows this lane copies: 4 rows x 8 lanes x 16 B per instruction, 16 times
+#pragma unroll
+      for (int i = 0; i < 16; ++i) crw[i] = coords[cslot * CH + lw * 64 + 4 * i + sub];
+      const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
+      for (int s = 0; s < NSLAB; ++s, ++sc) {
+        const uint32_t slot = sc % kRing;
+        if (!twait(&bars[B_EMPTY + slot], ((sc / kRing) & 1) ^ 1, abort_flag, p.status, 3, tracing,
+                   tr[TR_P_WAIT_EMPTY]))
+          return false;
+        const uint32_t slab = kv_base + slot * SLAB_BYTES;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int rl = 4 * i + sub;
+          const uint32_t dst = slab + (lw * 64 + rl) * 128 + ((c16 ^ (rl & 7)) << 4);
+          const bool v = crw[i] >= 0;
+          const uint8_t* src = pool + (size_t)(v ? crw[i] : 0) * (D * 2) + s * 128 + c16 * 16;
+          cp_async16(dst, src, v ? 16u : 0u);
+        }
+        cp_async_arrive(&bars[B_FULL + slot]);
+      }
+      return true;
+    };
     while (ok && wk.next(sg)) {
       if (tid == 0) {
         if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
@@ -1277,63 +1339,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, sg.t);
         }
       }
-      for (int c = sg.cb; ok && c < sg.ce; ++c, ++gchunk) {
-        const bool is_win = c < p.n_win_chunks;
-        const int slot = gchunk % CD;
-        if (!twait(&bars[B_CFULL + slot], (gchunk / CD) & 1, abort_flag, p.status, 3, tracing,
-                   tr[TR_P_WAIT_MASK])) {  // wait for the rows to be resolved
-          ok = false;
-          break;
-        }
-        // ---- rows this lane copies: 4 rows x 8 lanes x 16 B per instruction
-        int crw[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) crw[i] = coords[slot * CH + lw * 32 + 4 * i + sub];
-        const bool valid = (cmask[slot * 4 + lw] >> lane) & 1;
-        __syncwarp();
-        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + slot]);
-        const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
-        for (int s = 0; s < NSLAB; ++s) {
-          if (!twait(&bars[B_EMPTY + s], (gchunk & 1) ^ 1, abort_flag, p.status, 3, tracing,
-                     tr[TR_P_WAIT_EMPTY])) {
+      const int n_cmp = tokp[sg.t].n_cmp;
+      for (int k = sg.cb; ok && k < sg.ce; ++k) {
+        int c0, c1;
+        tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
+        const int nch = c1 - c0;
+        const uint32_t gch0 = gchunk;
+        for (int i = 0; ok && i < nch; ++i) {  // K rows
+          const uint32_t cs = (gch0 + i) % CD;
+          if (!twait(&bars[B_CFULL + cs], ((gch0 + i) / CD) & 1, abort_flag, p.status, 3, tracing,
+                     tr[TR_P_WAIT_MASK])) {  // wait for the rows to be resolved
             ok = false;
             break;
           }
-          const uint32_t slab = kv_base + s * SLAB_BYTES;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int rl = 4 * i + sub;
-            const uint32_t dst = slab + (lw * 32 + rl) * 128 + ((c16 ^ (rl & 7)) << 4);
-            const bool v = crw[i] >= 0;
-            const uint8_t* src = pool + (size_t)(v ? crw[i] : 0) * (D * 2) + s * 128 + c16 * 16;
-            cp_async16(dst, src, v ? 16u : 0u);
-          }
-          cp_async_arrive(&bars[B_FULL + s]);
+          ok = load_chunk(cs, c0 + i < p.n_win_chunks);
         }
-        if (!ok) break;
-        if (have_pend) {
-          have_pend = false;
-          if (!segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb)) {
-            ok = false;
-            break;
-          }
+        for (int i = 0; ok && i < nch; ++i) {  // V rows (the same rows again, mostly from L2)
+          ok = load_chunk((gch0 + i) % CD, c0 + i < p.n_win_chunks);
+          __syncwarp();
+          if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (gch0 + i) % CD]);
         }
-        if (!softmax_chunk<DT>(p, G, sm, bars, gchunk, c == sg.cb, valid, g, abort_flag, false, trb)) {
-          ok = false;
-          break;
-        }
+        gchunk += nch;
       }
-      pend = sg;
-      have_pend = true;
       ++seg_i;
     }
-    if (ok && have_pend) ok = segment_epilogue<DT>(p, G, sm, bars, pend, r, g, abort_flag, false, trb);
-    if (FUSED && ok)
-      zero_uncovered<DT>(p, G, usp, tokp,
-                         reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
-                         *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
+    // Per tile: S^T of every chunk into its own TMEM slot as the K rows land,
+    // then, per chunk, O^T += V^T P^T as the V rows land and P is ready.
     if (lane == 0) {
       constexpr uint32_t idesc1 = sas::umma_idesc_f16(DT == 0 ? 1 : 0, 128, HG, 0, 0);
       constexpr uint32_t idesc2 = sas::umma_idesc_f16(DT == 0 ? 1 : 0, 128, HG, 1, 1);
@@ -1343,107 +1376,131 @@ __global__ void __launch_bounds__(kThreads, 1)
       Walker wk;
       wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
       Seg sg;
-      uint32_t gchunk = 0, seg_i = 0;
+      uint32_t sc = 0, gp = 0, seg_i = 0;  // sc: ring slabs consumed so far, in the loaders' order
       bool ok = true;
       while (ok && wk.next(sg)) {
         if (!twait(&bars[B_QFULL], seg_i & 1, abort_flag, p.status, 4, tracing, tr[TR_M_WAIT_Q])) break;
-        for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
-          const bool first = c == sg.cb, last = c == sg.ce - 1;
+        const int n_cmp = tokp[sg.t].n_cmp;
+        for (int k = sg.cb; ok && k < sg.ce; ++k) {
+          int c0, c1;
+          tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
+          const int nch = c1 - c0;
           long long tg0 = 0;
-          // S^T = K . Q^T
-          for (int s = 0; s < NSLAB; ++s) {
-            if (!twait(&bars[B_FULL + s], gchunk & 1, abort_flag, p.status, 5, tracing, tr[TR_M_WAIT_FULL])) {
-              ok = false;
-              break;
-            }
-            sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
-            sas::tc_fence_after();
-            if (tracing && s == 0) tg0 = clock64();
+          // ---- S^T(i) = K(i) . Q^T
+          for (int i = 0; ok && i < nch; ++i) {
+            for (int s = 0; s < NSLAB; ++s, ++sc) {
+              const uint32_t slot = sc % kRing;
+              if (!twait(&bars[B_FULL + slot], (sc / kRing) & 1, abort_flag, p.status, 5, tracing,
+                         tr[TR_M_WAIT_FULL])) {
+                ok = false;
+                break;
+              }
+              sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
+              sas::tc_fence_after();
+              if (tracing && i == 0 && s == 0) tg0 = clock64();
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t ad = sas::umma_desc_sw128(kv_base + s * SLAB_BYTES + kk * 32, 16, 1024);
-              const uint64_t bd = sas::umma_desc_sw128(q_base + s * Q_SLAB_BYTES + kk * 32, 16, 1024);
-              sas::umma_ss(tmem + TM_S, ad, bd, idesc1, (s | kk) != 0);
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 32, 16, 1024);
+                const uint64_t bd = sas::umma_desc_sw128(q_base + s * Q_SLAB_BYTES + kk * 32, 16, 1024);
+                sas::umma_ss(tmem + TM_S + 64 * i, ad, bd, idesc1, (s | kk) != 0);
+              }
+              sas::umma_commit(&bars[B_EMPTY + slot]);
             }
           }
           if (!ok) break;
           sas::umma_commit(&bars[B_SFULL]);
-          if (last) sas::umma_commit(&bars[B_QEMPTY]);
-          if (tracing) {  // diagnostics only: G1 latency, first issue to completion
-            unsigned long long dummy = 0;
-            twait(&bars[B_SFULL], gchunk & 1, abort_flag, p.status, 4, false, dummy);
-            tr[TR_M_WAIT_O] += clock64() - tg0;
-          }
-          // O^T += V^T . P^T
-          if (!twait(&bars[B_PREADY], gchunk & 1, abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P])) {
-            ok = false;
-            break;
-          }
-          if (first && seg_i > 0) {
-            if (!twait(&bars[B_OEMPTY], (seg_i - 1) & 1, abort_flag, p.status, 7, tracing, tr[TR_M_WAIT_O])) {
+          if (k == sg.ce - 1) sas::umma_commit(&bars[B_QEMPTY]);
+          if (tracing) tr[TR_M_WAIT_O] += clock64() - tg0;
+          // ---- O^T += V^T(i) . P^T(i)
+          for (int i = 0; ok && i < nch; ++i) {
+            const bool first = k == sg.cb && i == 0;
+            if (!twait(&bars[B_PREADY2 + (gp & 1)], (gp >> 1) & 1, abort_flag, p.status, 6, tracing,
+                       tr[TR_M_WAIT_P])) {
               ok = false;
               break;
             }
-          }
-          sas::tc_fence_after();
-          if (tracing) tg0 = clock64();
-#pragma unroll 1
-          for (int j = 0; j < 4; ++j) {
-#pragma unroll
-            for (int kk = 0; kk < 8; ++kk) {
-              const uint64_t ad = sas::umma_desc_sw128(kv_base + (2 * j) * SLAB_BYTES + kk * 2048, SLAB_BYTES, 1024);
-              const uint64_t bd = sas::umma_desc_sw128(p_base + kk * 2048, 8192, 1024);
-              sas::umma_ss(tmem + TM_O + 64 * j, ad, bd, idesc2, (first && kk == 0) ? 0u : 1u);
+            if (first && seg_i > 0 &&
+                !twait(&bars[B_OEMPTY], (seg_i - 1) & 1, abort_flag, p.status, 7, tracing, tr[TR_M_WAIT_O])) {
+              ok = false;
+              break;
             }
-            sas::umma_commit(&bars[B_EMPTY + 2 * j]);
-            sas::umma_commit(&bars[B_EMPTY + 2 * j + 1]);
+            sas::tc_fence_after();
+            const uint32_t pb = p_base + (gp & 1) * P_BYTES;
+            for (int j = 0; j < 4; ++j, sc += 2) {
+              const uint32_t slot = sc % kRing;  // even: the pair (slot, slot + 1) never wraps
+              const uint32_t par = (sc / kRing) & 1;
+              if (!twait(&bars[B_FULL + slot], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL]) ||
+                  !twait(&bars[B_FULL + slot + 1], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL])) {
+                ok = false;
+                break;
+              }
+              sas::fence_proxy_async_smem();
+              sas::tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 2048, SLAB_BYTES, 1024);
+                const uint64_t bd = sas::umma_desc_sw128(pb + kk * 2048, 8192, 1024);
+                sas::umma_ss(tmem + TM_O + 64 * j, ad, bd, idesc2, (first && kk == 0) ? 0u : 1u);
+              }
+              sas::umma_commit(&bars[B_EMPTY + slot]);
+              sas::umma_commit(&bars[B_EMPTY + slot + 1]);
+            }
+            if (!ok) break;
+            sas::umma_commit(&bars[B_PFREE + (gp & 1)]);
+            ++gp;
           }
-          if (last) sas::umma_commit(&bars[B_OFULL]);
-          if (tracing) {  // diagnostics only: G2 latency
-            unsigned long long dummy = 0;
-            twait(&bars[B_EMPTY + NSLAB - 1], gchunk & 1, abort_flag, p.status, 4, false, dummy);
-            tr[TR_E_COPY] += clock64() - tg0;
-          }
+          if (ok && k == sg.ce - 1) sas::umma_commit(&bars[B_OFULL]);
         }
         ++seg_i;
       }
     }
     __syncwarp();
-  } else if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarp0 + 4) {
-    // =============================== softmax group A (heads 0-31) / epilogue
+  } else if (warp >= kSoftmaxWarp0) {
+    // =============================== softmax groups A (warps 4-7, heads 0-31)
+    // and B (warps 8-11, heads 32-63) / epilogue
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
-    SmGroup G{0, 0, quad, lane, quad * 32 + lane, quad == 0,
-              GroupSync{&bars[B_SSYNC], reinterpret_cast<uint32_t*>(misc + M_SWORD), 0}, {},
-              tmem + ((uint32_t)(quad * 32) << 16), 0};
+    const int half = warp >= kSoftmaxWarpB ? 1 : 0;
+    SmGroup G{32 * half, half, quad, lane, quad * 32 + lane, quad == 0,
+              GroupSync{&bars[half ? B_LSYNC : B_SSYNC], reinterpret_cast<uint32_t*>(misc + (half ? M_LWORD : M_SWORD)),
+                        0},
+              {}, tmem + ((uint32_t)(quad * 32) << 16), 0};
     Walker wk;
     wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Seg sg;
-    uint32_t gchunk = 0;
+    uint32_t gchunk = 0, gtile = 0, gp = 0;
     bool ok = true;
+    const bool trace_me = tracing && half == 0;
+    unsigned long long trb[TR_NSLOTS];
+    unsigned long long* trp = half == 0 ? tr : trb;
     while (ok && wk.next(sg)) {
-      for (int c = sg.cb; c < sg.ce; ++c, ++gchunk) {
-        const int cslot = gchunk % CD;
-        if (!twait(&bars[B_CFULL + cslot], (gchunk / CD) & 1, abort_flag, p.status, 8, tracing,
-                   tr[TR_S_WAIT_MASK])) {
-          ok = false;
-          break;
+      const int n_cmp = tokp[sg.t].n_cmp;
+      for (int k = sg.cb; ok && k < sg.ce; ++k) {
+        int c0, c1;
+        tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
+        const int nch = c1 - c0;
+        const uint32_t gch0 = gchunk;
+        for (int i = 0; ok && i < nch; ++i)  // the tile's validity masks
+          ok = twait(&bars[B_CFULL + (gch0 + i) % CD], ((gch0 + i) / CD) & 1, abort_flag, p.status, 8, trace_me,
+                     trp[TR_S_WAIT_MASK]);
+        float al;
+        int need;
+        if (ok)
+          ok = tile_max_pass<DT>(p, G, sm, bars, cmask, gtile, gch0, nch, k == sg.cb, g, al, need, abort_flag,
+                                 trace_me, trp);
+        for (int i = 0; ok && i < nch; ++i) {
+          ok = chunk_exp_pass<DT>(p, G, sm, bars, cmask, gch0 + i, i, i == 0 && need, k == sg.cb, al, gp,
+                                  abort_flag, trace_me, trp);
+          __syncwarp();
+          if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (gch0 + i) % CD]);
         }
-        const bool valid = (cmask[cslot * 4 + quad] >> lane) & 1;
-        __syncwarp();
-        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + cslot]);
-        if (!softmax_chunk<DT>(p, G, sm, bars, gchunk, c == sg.cb, valid, g, abort_flag, tracing, tr)) {
-          ok = false;
-          break;
-        }
-        if (c == sg.ce - 1 && !segment_epilogue<DT>(p, G, sm, bars, sg, r, g, abort_flag, tracing, tr)) {
-          ok = false;
-          break;
-        }
+        gchunk += nch;
+        ++gtile;
+        if (ok && k == sg.ce - 1)
+          ok = segment_epilogue<DT>(p, G, sm, bars, sg, r, g, abort_flag, trace_me, trp);
       }
     }
     if (FUSED && ok)
-      zero_uncovered<DT>(p, G, usp, tokp,
-                         reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
+      zero_uncovered<DT>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   }
 
@@ -1538,7 +1595,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 }
 
 // Tuning / diagnostics knobs set through sas_fwd_set_option (process-wide).
-float g_tau = 8.0f;
+float g_tau = 0.0f;  // exact running max (golden.py); > 0 only for experiments
 unsigned long long* g_trace = nullptr;
 
 struct WsLayout {

@@ -70,6 +70,7 @@ def test_attention_vs_reference_fixtures(i):
     case = U.build_case(cfg)
     out, lse = U.run_api(case)
     U.check_close(out, ref_out, lse, ref_lse, what=cfg["name"])
+    U.check_result_ref(out, ref_out, case.dtype)
     U.check_lse_ref(lse, ref_lse, case.dtype)
 
 

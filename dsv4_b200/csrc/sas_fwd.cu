@@ -67,7 +67,8 @@ constexpr int kCoordWarp = 3;           // warp 3: row resolution + L2 prefetch,
 constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax group A (heads 0-31) / epilogue
 constexpr int kSoftmaxWarpB = 8;        // warps 8-11: softmax group B (heads 32-63) / epilogue
 constexpr int kThreads = 32 * 12;
-constexpr int CD = 4;                    // depth of the row-coordinate ring (chunks)
+constexpr int kTileChunksC = 4;          // chunks per softmax tile (512 rows)
+constexpr int CD = 2 * kTileChunksC;     // depth of the row-coordinate ring (chunks): two tiles
 // Chunks a token may hold beyond a range's length before it is cut across
 // ranges: a cut costs the partial write-back and the merge, about this many
 // chunks of work.
@@ -77,7 +78,7 @@ constexpr int kCutCost = 1;  // in units (tiles)
 // tiles of 512, i.e. up to kTileChunks 128-row chunks. The running max is
 // updated once per tile with the tile's exact max, so P is rounded at the
 // same points as the reference.
-constexpr int kTileChunks = 4;
+constexpr int kTileChunks = kTileChunksC;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -93,19 +94,20 @@ constexpr int OFF_KV = OFF_Q + NSLAB * Q_SLAB_BYTES;     // 64 KB
 constexpr int OFF_P = OFF_KV + kRing * SLAB_BYTES;       // +96 KB
 constexpr int OFF_MISC = OFF_P + 2 * P_BYTES;            // +32 KB (double-buffered P^T)
 // misc region
-constexpr int M_BAR = 0;         // 40 mbarriers x 8 B
-constexpr int M_TMEM = 320;      // tmem base address
-constexpr int M_ABORT = 324;
-constexpr int M_CMASK = 336;     // CD x 4 words: row-validity mask per ring slot
-constexpr int M_LWORD = 400;     // 3 words: group B (loader warps) OR
-constexpr int M_SWORD = 416;     // 3 words: group A (softmax warps) OR
+constexpr int M_BAR = 0;         // 48 mbarriers x 8 B
+constexpr int M_TMEM = 384;      // tmem base address
+constexpr int M_ABORT = 388;
+constexpr int M_LWORD = 400;     // 3 words: group B (softmax warps 8-11) OR
+constexpr int M_SWORD = 416;     // 3 words: group A (softmax warps 4-7) OR
 constexpr int M_RANGE = 432;     // RangeInfo of this CTA (4 ints)
-constexpr int M_RED = 512;       // [2 chunk parities][4 quads][64 heads] per-warp maxima, 2 KB
-constexpr int M_MRUN = 2560;     // [2 groups][4 quads][32 heads] each warp's running max, 1 KB
-constexpr int M_INV = 3584;      // 64 floats: 1/l
-constexpr int M_LRED = 3840;     // [4 quads][64 heads] per-warp row sums (epilogue), 1 KB
-constexpr int M_COORD = 4864;    // CD x 128 int32: pool row per chunk row (-1 = masked)
-constexpr int M_MW = M_COORD + CD * CH * 4;  // kTmemMergeMax x 64 floats: merge weights
+constexpr int M_CMASK = 448;     // CD x 4 words: row-validity mask per ring slot
+constexpr int M_RED = M_CMASK + CD * 16;  // [2 tile parities][4 quads][64 heads] per-warp maxima, 2 KB
+constexpr int M_MRUN = M_RED + 2048;      // [2 groups][4 quads][32 heads] each warp's running max, 1 KB
+constexpr int M_INV = M_MRUN + 1024;      // 64 floats: 1/l
+constexpr int M_LRED = M_INV + 256;       // [4 quads][64 heads] per-warp row sums (epilogue), 1 KB
+constexpr int M_COORD = M_LRED + 1024;    // CD x 128 int32: pool row per chunk row (-1 = masked)
+constexpr int M_CINFO = M_COORD + CD * CH * 4;  // CD x int2: chunk flags and token (ChunkFlag)
+constexpr int M_MW = M_CINFO + CD * 8;           // kTmemMergeMax x 64 floats: merge weights
 constexpr int kTmemMergeMax = 4;                 // pieces merged straight from TMEM (else via L2)
 constexpr int MISC_BYTES = M_MW + kTmemMergeMax * 64 * 4;
 constexpr int kFusedMaxT = 512;  // token plans built inside the attention kernel (no plan kernel)
@@ -123,7 +125,6 @@ constexpr int B_FULL = 0;        // kRing
 constexpr int B_EMPTY = 8;       // kRing
 constexpr int B_QFULL = 16;
 constexpr int B_QEMPTY = 17;
-constexpr int B_SFULL = 18;
 constexpr int B_OFULL = 20;
 constexpr int B_OEMPTY = 21;
 // Per P^T buffer b (chunk n uses buffer n % 2), so that each completes once per
@@ -131,12 +132,25 @@ constexpr int B_OEMPTY = 21;
 constexpr int B_PREADY2 = 32;    // 2: P^T(n) written by both softmax groups (256 arrivals)
 constexpr int B_PFREE = 34;      // 2: P.V(n) done, buffer n % 2 may be rewritten
 constexpr int B_CFULL = 22;      // CD: coordinate ring slot written
-constexpr int B_LSYNC = 26;      // group barrier of softmax group B (warps 0-3)
-constexpr int B_SSYNC = 27;      // group barrier of softmax group A (warps 4-7)
-constexpr int B_CEMPTY = 28;     // CD: slot read by the 4 loader and 4 softmax warps
+constexpr int B_LSYNC = 30;      // group barrier of softmax group B (warps 8-11)
+constexpr int B_SSYNC = 31;      // group barrier of softmax group A (warps 4-7)
+constexpr int B_CEMPTY = 36;     // CD: slot done with by the loader warps, the softmax warps and the MMA
+constexpr int B_SF = 44;         // kTileChunks: S^T of chunk n landed in TMEM slot n % kTileChunks
+static_assert(B_CFULL + CD <= B_LSYNC && B_CEMPTY + CD <= B_SF && B_SF + kTileChunks <= 48, "barrier map");
+constexpr int kCemptyCount = kLoaderWarps + 8 + 1;  // loader warps + softmax warps + the MMA thread
+
+// Per-chunk flags published by the coordinate warp with the chunk's rows
+// (int2 {flags, token} per coordinate-ring slot).
+enum ChunkFlag : int {
+  CF_END = 1,         // no chunk: the stream has ended
+  CF_WIN = 2,         // window chunk (ori pool), else compressed
+  CF_SEG_FIRST = 4,   // first chunk of a segment
+  CF_SEG_LAST = 8,    // last chunk of a segment
+  CF_TILE_LAST = 16,  // last chunk of a softmax tile
+};
 
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t TM_S = 0;     // S^T of the tile's chunks: kTileChunks slots of 64 columns
+constexpr uint32_t TM_S = 0;     // S^T: kTileChunks slots of 64 columns, chunk n in slot n % kTileChunks
 constexpr uint32_t TM_O = 256;   // O^T: 4 d-tiles of 64 columns
 
 struct TokInfo {
@@ -412,6 +426,51 @@ struct Walker {
   }
 };
 
+// One tile of this CTA's work in stream order (tiles of consecutive segments).
+struct Tile {
+  int t, c0, nch;
+  uint32_t seg, g0;  // segment number; global number of the tile's first chunk
+  bool first, last;  // first / last tile of its segment
+};
+
+// Walks this CTA's tiles across segment boundaries, so that the copy and MMA
+// roles can look one tile ahead.
+struct TileIter {
+  Walker wk;
+  Seg sg;
+  int k, n_cmp;
+  uint32_t seg, g;
+  bool started;
+  __device__ void init(const int32_t* unit_start, const RangeInfo& ri) {
+    wk.init(unit_start, ri);
+    started = false;
+    seg = 0;
+    g = 0;
+    k = 0;
+    sg.ce = 0;
+  }
+  __device__ bool next(Tile& tl, const TokInfo* tokp, int n_win_chunks) {
+    if (!started || k >= sg.ce) {
+      if (!wk.next(sg)) return false;
+      if (started) ++seg;
+      started = true;
+      k = sg.cb;
+      n_cmp = tokp[sg.t].n_cmp;
+    }
+    int c1;
+    tile_chunks(k, n_win_chunks, n_cmp, tl.c0, c1);
+    tl.t = sg.t;
+    tl.nch = c1 - tl.c0;
+    tl.seg = seg;
+    tl.g0 = g;
+    tl.first = k == sg.cb;
+    tl.last = k == sg.ce - 1;
+    g += tl.nch;
+    ++k;
+    return true;
+  }
+};
+
 template <int DT>
 struct IoType;
 template <>
@@ -471,6 +530,37 @@ __device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, volatile i
   if (tracing) acc += clock64() - t0;
   return r;
 }
+
+// The order in which the loaders copy, and the MMA issuer consumes, the two
+// passes over every chunk n: K(n), the rows for S^T = K Q^T, and V(n), the
+// same rows again for O^T += V^T P^T. Both roles step this rule in lockstep
+// (it depends only on the chunk flags the coordinate warp publishes):
+//  - K(n) as soon as n <= nv + 4: S^T(n) goes to TMEM slot n % 4, free once
+//    the exp pass of chunk n - 4 has read it, and that exp pass needs only
+//    stream items before K(n) (the S^T of its tile, P.V of chunks n - 6 and
+//    n - 5);
+//  - else V(nv), which needs the tile's max, i.e. every K of its tile.
+// The scores of the next tiles are therefore computed while P.V of the
+// current one runs, across token boundaries.
+enum StreamItem { SI_K = 0, SI_V = 1, SI_END = 2, SI_FAIL = 3 };
+struct Stream {
+  uint32_t nk = 0, nv = 0;  // next chunk for K, for V
+  bool kend = false;        // every chunk has had its K
+  template <bool TR>
+  __device__ __forceinline__ int next(uint64_t* bars, const int2* cinfo, volatile int* abort_flag, int* status,
+                                      unsigned long long& tslot) {
+    if (!kend && nk <= nv + kTileChunks) {
+      if (!twait(&bars[B_CFULL + nk % CD], (nk / CD) & 1, abort_flag, status, 3, TR, tslot)) return SI_FAIL;
+      if (!(cinfo[nk % CD].x & CF_END)) return SI_K;
+      kend = true;
+    }
+    if (nv == nk) return SI_END;  // only once kend: else K(nk) was taken above
+    if (kend) return SI_V;
+    for (uint32_t j = nv; j < nk; ++j)
+      if (cinfo[j % CD].x & CF_TILE_LAST) return SI_V;
+    return SI_FAIL;  // unreachable: nk > nv + 4 spans a whole tile
+  }
+};
 
 // Barrier among the 4 warps of one role, with a bounded wait (a named
 // barrier cannot time out, and a sibling warp that left on an abort would
@@ -644,17 +734,21 @@ __device__ __forceinline__ bool tile_max_pass(const FwdParams& p, SmGroup& G, co
 #pragma unroll
     for (int h2 = 0; h2 < 32; ++h2) G.lsum[h2] = 0.f;
   }
-  if (!twait(&bars[B_SFULL], gtile & 1, abort_flag, p.status, 9, tracing, tr[TR_S_WAIT_S])) return false;
-  sas::tc_fence_after();
-  const long long ts0 = tracing ? clock64() : 0;
+  long long ts0 = 0;
   float mx[32];
 #pragma unroll
   for (int h = 0; h < 32; ++h) mx[h] = -INFINITY;
 #pragma unroll 1
   for (int i = 0; i < nch; ++i) {
-    const bool valid = (cmask[((gch0 + i) % CD) * 4 + G.quad] >> G.lane) & 1;
+    const uint32_t n = gch0 + i;
+    if (!twait(&bars[B_SF + n % kTileChunks], (n / kTileChunks) & 1, abort_flag, p.status, 9, tracing,
+               tr[TR_S_WAIT_S]))
+      return false;
+    sas::tc_fence_after();
+    if (tracing && i == 0) ts0 = clock64();
+    const bool valid = (cmask[(n % CD) * 4 + G.quad] >> G.lane) & 1;
     uint32_t ra[32];
-    sas::tmem_ld32(G.lane_addr + TM_S + 64 * i + G.hb, ra);
+    sas::tmem_ld32(G.lane_addr + TM_S + 64 * (n % kTileChunks) + G.hb, ra);
     sas::tmem_wait_ld();
     if (valid) {
 #pragma unroll
@@ -704,7 +798,7 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
   float x[32];
   {
     uint32_t ra[32];
-    sas::tmem_ld32(G.lane_addr + TM_S + 64 * i + G.hb, ra);
+    sas::tmem_ld32(G.lane_addr + TM_S + 64 * (gchunk % kTileChunks) + G.hb, ra);
     sas::tmem_wait_ld();
 #pragma unroll
     for (int h = 0; h < 32; ++h) x[h] = valid ? sas::ex2(__uint_as_float(ra[h]) * p.scale_log2 - mw[h]) : 0.f;
@@ -967,6 +1061,76 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
   return true;
 }
 
+// A complete token's epilogue in two halves, so that the softmax groups can
+// start the next token's first tile in between (its max pass and first exp
+// pass overlap the last P.V of this token):
+//  - first half, before the next tile: l over the 4 quads, 1/l with the sink
+//    folded in, lse (golden.py:201-205); needs only this thread's sums and
+//    the running max, not O^T;
+//  - second half, after it: O^T / l from TMEM to the output rows, then O^T is
+//    released to the MMA.
+// The next tile's max pass holds a group barrier, which orders the first
+// half's shared-memory writes before the second half's reads.
+template <int DT>
+__device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup& G, const SmShared& S, const Seg& sg,
+                                                    int g, volatile int* abort_flag) {
+  float l[32];
+#pragma unroll
+  for (int h = 0; h < 32; ++h) l[h] = G.lsum[h];
+  warp_reduce_scatter<32, false>(l, G.lane);
+  S.lred[G.quad * 64 + G.hb + G.lane] = l[0];
+  if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 18)) return false;
+  if (G.gst < 32) {
+    const int c = G.hb + G.gst, h = g * HG + c;
+    const float L = S.lred[c] + S.lred[64 + c] + S.lred[128 + c] + S.lred[192 + c];
+    const float m = warp_mrun(S, G)[G.gst];  // threads 0-31 are the quad-0 warp
+    const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
+    const float Lf = L + sas::ex2(sink - m);
+    S.inv[c] = 1.f / Lf;
+    if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+  }
+  return true;
+}
+
+template <int DT>
+__device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup& G, const SmShared& S,
+                                                     uint64_t* bars, const Seg& sg, int g, volatile int* abort_flag,
+                                                     bool tracing, unsigned long long* tr) {
+  using IO = IoType<DT>;
+  if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
+  sas::tc_fence_after();
+  const long long te0 = tracing ? clock64() : 0;
+  // direct stores: lanes pair up (row, row^1); the even lane stores head h
+  // for both rows, the odd lane head h+16
+  const int row = G.gst;  // d within an O^T tile
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
+  const bool odd = G.lane & 1;
+  const int d_even = row & ~1;
+#pragma unroll 1
+  for (int j = 0; j < 4; ++j) {
+    uint32_t o[32];
+    sas::tmem_ld32(G.lane_addr + TM_O + 64 * j + G.hb, o);
+    sas::tmem_wait_ld();
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      const float v0 = __uint_as_float(o[h]) * S.inv[G.hb + h];
+      const float v1 = __uint_as_float(o[h + 16]) * S.inv[G.hb + h + 16];
+      const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+      const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
+      const int hh = g * HG + G.hb + (odd ? h + 16 : h);
+      if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+    }
+  }
+  sas::tc_fence_before();
+  sas::mbar_arrive(&bars[B_OEMPTY]);
+  ++G.seg;
+  if (tracing) {
+    tr[TR_S_EPI] += clock64() - te0;
+    tr[TR_SEGS] += 1;
+  }
+  return true;
+}
+
 // Fused plan: metadata coverage (kernel.py:254-278 windows) is checked after
 // the fact. Every token with work was written as if covered; once the
 // metadata is complete, each softmax group walks its range again and zeroes
@@ -1119,6 +1283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + M_TMEM);
   uint32_t* cmask = reinterpret_cast<uint32_t*>(misc + M_CMASK);        // [CD][4]
   int32_t* coords = reinterpret_cast<int32_t*>(misc + M_COORD);          // [CD][128]
+  int2* cinfo = reinterpret_cast<int2*>(misc + M_CINFO);                 // [CD] {ChunkFlag bits, token}
   float* red = reinterpret_cast<float*>(misc + M_RED);
   float* m_run = reinterpret_cast<float*>(misc + M_MRUN);
   float* inv_s = reinterpret_cast<float*>(misc + M_INV);
@@ -1140,7 +1305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sas::mbar_init(&bars[B_QFULL], 1);
     sas::mbar_init(&bars[B_QEMPTY], 1);
-    sas::mbar_init(&bars[B_SFULL], 1);
+    for (int i = 0; i < kTileChunks; ++i) sas::mbar_init(&bars[B_SF + i], 1);
     sas::mbar_init(&bars[B_OFULL], 1);
     sas::mbar_init(&bars[B_OEMPTY], 256);
     for (int i = 0; i < 2; ++i) {
@@ -1149,7 +1314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < CD; ++i) {
       sas::mbar_init(&bars[B_CFULL + i], 1);
-      sas::mbar_init(&bars[B_CEMPTY + i], kLoaderWarps + 8);
+      sas::mbar_init(&bars[B_CEMPTY + i], kCemptyCount);
     }
     sas::mbar_init(&bars[B_SSYNC], 4);
     sas::mbar_init(&bars[B_LSYNC], 4);
@@ -1198,96 +1363,128 @@ __global__ void __launch_bounds__(kThreads, 1)
     // block tables (kernel.py:285-401, 686-766), writes the pool row (or -1)
     // and the validity mask into the ring, and starts each valid row on its
     // way into L2, so the loaders' copies later hit L2.
-    Walker wk;
-    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
-    Seg sg;
-    uint32_t gchunk = 0;
-    bool ok = true;
-    while (ok && wk.next(sg)) {
-      const TokInfo ti = tokp[sg.t];
-      int cb_c, ce_c, dummy;  // the segment's chunk range
-      tile_chunks(sg.cb, p.n_win_chunks, ti.n_cmp, cb_c, dummy);
-      tile_chunks(sg.ce - 1, p.n_win_chunks, ti.n_cmp, dummy, ce_c);
-      // the compressed scan stops at the first -1 (golden.py:55-56): a range
-      // that starts inside a token looks for one in the slots before it
-      bool stopped = false;
-      const int cmp_c0 = max(cb_c - p.n_win_chunks, 0);
-      if (p.scenario == 3 && cmp_c0 > 0) {
-        const int lim = min(cmp_c0 * CH, ti.n_cmp);
-        const int32_t* ip = p.idx + (size_t)sg.t * p.K;
-        int neg = 0;
-        for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
-        stopped = __any_sync(0xffffffffu, neg);
+    // A whole tile (up to 4 chunks) is resolved per round with all its loads
+    // in flight together: the index rows, then the block-table entries.
+    TileIter it;
+    it.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    Tile tl;
+    TokInfo ti{};
+    bool stopped = false, ok = true;
+    while (ok && it.next(tl, tokp, p.n_win_chunks)) {
+      const long long tc0 = tracing ? clock64() : 0;
+      if (tl.first) {
+        ti = tokp[tl.t];
+        // the compressed scan stops at the first -1 (golden.py:55-56): a range
+        // that starts inside a token looks for one in the slots before it
+        stopped = false;
+        const int cmp_c0 = max(tl.c0 - p.n_win_chunks, 0);
+        if (p.scenario == 3 && cmp_c0 > 0) {
+          const int lim = min(cmp_c0 * CH, ti.n_cmp);
+          const int32_t* ip = p.idx + (size_t)tl.t * p.K;
+          int neg = 0;
+          for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
+          stopped = __any_sync(0xffffffffu, neg);
+        }
       }
-      for (int c = cb_c; c < ce_c; ++c, ++gchunk) {
-        const long long tc0 = tracing ? clock64() : 0;
-        const bool is_win = c < p.n_win_chunks;
-        const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
-        int coord[4];
-        bool val[4];
-        if (is_win) {
-          const int lo = max(ti.s_g - p.win_left, 0);
+      const bool is_win = tl.c0 < p.n_win_chunks;  // a tile is all window or all compressed
+      const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
+      int coord[kTileChunks][4];
+      bool val[kTileChunks][4];
+      if (is_win) {
+        const int lo = max(ti.s_g - p.win_left, 0);
+#pragma unroll
+        for (int j = 0; j < kTileChunks; ++j)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int pos = lo + c * CH + k * 32 + lane;
-            val[k] = (ti.s_g >= 0) && pos <= ti.s_g;
-            const int blk = val[k] ? p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs] : -1;
-            val[k] = val[k] && blk >= 0;
-            coord[k] = blk * p.ori_bs + pos % p.ori_bs;
+            const int pos = lo + (tl.c0 + j) * CH + k * 32 + lane;
+            val[j][k] = j < tl.nch && ti.s_g >= 0 && pos <= ti.s_g;
+            const int blk = val[j][k] ? p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs] : -1;
+            val[j][k] = val[j][k] && blk >= 0;
+            coord[j][k] = blk * p.ori_bs + pos % p.ori_bs;
           }
-        } else {
-          int id[4];
+      } else {
+        const int e0 = (tl.c0 - p.n_win_chunks) * CH;
+#pragma unroll
+        for (int j = 0; j < kTileChunks; ++j)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const int e = (c - p.n_win_chunks) * CH + k * 32 + lane;
-            val[k] = e < ti.n_cmp;
-            id[k] = e;
-            if (p.scenario == 3) id[k] = val[k] ? p.idx[(size_t)sg.t * p.K + e] : 0;
+            const int e = e0 + j * CH + k * 32 + lane;
+            val[j][k] = j < tl.nch && e < ti.n_cmp;
+            coord[j][k] = e;  // the compressed id, until resolved
+            if (p.scenario == 3) coord[j][k] = val[j][k] ? p.idx[(size_t)tl.t * p.K + e] : 0;
           }
-          if (p.scenario == 3) {
+        if (p.scenario == 3) {
+#pragma unroll
+          for (int j = 0; j < kTileChunks; ++j) {
             int cf = CH;  // first -1 of this chunk, in row order
 #pragma unroll
             for (int k = 3; k >= 0; --k) {
-              const unsigned bal = __ballot_sync(0xffffffffu, val[k] && id[k] == -1);
+              const unsigned bal = __ballot_sync(0xffffffffu, val[j][k] && coord[j][k] == -1);
               if (bal) cf = k * 32 + __ffs(bal) - 1;
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              val[k] = val[k] && !stopped && k * 32 + lane < cf && id[k] >= 0 && id[k] < ti.thr;
-            stopped = stopped || cf < CH;
-          } else {
-#pragma unroll
-            for (int k = 0; k < 4; ++k) val[k] = val[k] && id[k] < ti.thr;
+              val[j][k] = val[j][k] && !stopped && k * 32 + lane < cf && coord[j][k] >= 0 && coord[j][k] < ti.thr;
+            stopped = stopped || (j < tl.nch && cf < CH);
           }
+        } else {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int blk = val[k] ? p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id[k] / p.cmp_bs] : -1;
-            val[k] = val[k] && blk >= 0;
-            coord[k] = val[k] ? blk * p.cmp_bs + id[k] % p.cmp_bs : 0;
-          }
+          for (int j = 0; j < kTileChunks; ++j)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) val[j][k] = val[j][k] && coord[j][k] < ti.thr;
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (val[k]) {
-            const uint8_t* rp = pool + (size_t)coord[k] * (D * 2);
+        for (int j = 0; j < kTileChunks; ++j)
 #pragma unroll
-            for (int l = 0; l < 8; ++l) sas::prefetch_l2_line(rp + l * 128);
+          for (int k = 0; k < 4; ++k) {
+            const int id = coord[j][k];
+            const int blk = val[j][k] ? p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id / p.cmp_bs] : -1;
+            val[j][k] = val[j][k] && blk >= 0;
+            coord[j][k] = val[j][k] ? blk * p.cmp_bs + id % p.cmp_bs : 0;
           }
-        if (tracing) tr[TR_P_COORD] += clock64() - tc0;
-        const int slot = gchunk % CD;
-        if (!twait(&bars[B_CEMPTY + slot], ((gchunk / CD) & 1) ^ 1, abort_flag, p.status, 2, tracing,
+      }
+      if (tracing) tr[TR_P_COORD] += clock64() - tc0;
+#pragma unroll
+      for (int j = 0; j < kTileChunks; ++j) {
+        if (j >= tl.nch) break;
+        const uint32_t gc = tl.g0 + j;
+        const int slot = gc % CD;
+        if (!twait(&bars[B_CEMPTY + slot], ((gc / CD) & 1) ^ 1, abort_flag, p.status, 2, tracing,
                    tr[TR_P_WAIT_MASK])) {
           ok = false;
           break;
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          coords[slot * CH + k * 32 + lane] = val[k] ? coord[k] : -1;
-          const unsigned vb = __ballot_sync(0xffffffffu, val[k]);
+          coords[slot * CH + k * 32 + lane] = val[j][k] ? coord[j][k] : -1;
+          const unsigned vb = __ballot_sync(0xffffffffu, val[j][k]);
           if (lane == 0) cmask[slot * 4 + k] = vb;
+        }
+        if (lane == 0) {
+          const int fl = (is_win ? CF_WIN : 0) | (tl.first && j == 0 ? CF_SEG_FIRST : 0) |
+                         (tl.last && j == tl.nch - 1 ? CF_SEG_LAST : 0) | (j == tl.nch - 1 ? CF_TILE_LAST : 0);
+          cinfo[slot] = make_int2(fl, tl.t);
         }
         __syncwarp();
         if (lane == 0) sas::mbar_arrive(&bars[B_CFULL + slot]);
+        // start the chunk's rows on their way into L2 for the loaders
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (val[j][k]) {
+            const uint8_t* rp = pool + (size_t)coord[j][k] * (D * 2);
+#pragma unroll
+            for (int l = 0; l < 8; ++l) sas::prefetch_l2_line(rp + l * 128);
+          }
+      }
+    }
+    if (ok) {  // the end of the stream, as one more ring slot
+      const uint32_t gc = it.g;
+      const int slot = gc % CD;
+      if (twait(&bars[B_CEMPTY + slot], ((gc / CD) & 1) ^ 1, abort_flag, p.status, 2, tracing, tr[TR_P_WAIT_MASK])) {
+        if (lane == 0) {
+          cinfo[slot] = make_int2(CF_END, 0);
+          sas::mbar_arrive(&bars[B_CFULL + slot]);
+        }
       }
     }
   } else if (warp < kLoaderWarps) {
@@ -1298,10 +1495,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int lw = warp;  // rows [64*lw, 64*lw+64) of every chunk
     const int sub = lane >> 3, c16 = lane & 7;
     const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
-    Walker wk;
-    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
-    Seg sg;
-    uint32_t sc = 0, gchunk = 0, seg_i = 0;  // sc: ring slabs filled so far
+    uint32_t sc = 0;  // ring slabs filled so far
     const uint32_t q_bytes = (uint32_t)NSLAB * p.q_box_h * 128;
     bool ok = true;
     // copy the 128 rows of chunk-slot `cslot` (pool rows resolved by the
@@ -1329,39 +1523,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       return true;
     };
-    while (ok && wk.next(sg)) {
-      if (tid == 0) {
-        if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
-          ok = false;
-        } else {
-          sas::mbar_arrive_expect_tx(&bars[B_QFULL], q_bytes);
-          for (int s = 0; s < NSLAB; ++s)
-            sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, sg.t);
-        }
+    Stream st;
+    uint32_t seg_i = 0;
+    while (ok) {
+      const int item = st.next<tracing>(bars, cinfo, abort_flag, p.status, tr[TR_P_WAIT_MASK]);
+      if (item == SI_END) break;
+      if (item == SI_FAIL) {
+        ok = false;
+        break;
       }
-      const int n_cmp = tokp[sg.t].n_cmp;
-      for (int k = sg.cb; ok && k < sg.ce; ++k) {
-        int c0, c1;
-        tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
-        const int nch = c1 - c0;
-        const uint32_t gch0 = gchunk;
-        for (int i = 0; ok && i < nch; ++i) {  // K rows
-          const uint32_t cs = (gch0 + i) % CD;
-          if (!twait(&bars[B_CFULL + cs], ((gch0 + i) / CD) & 1, abort_flag, p.status, 3, tracing,
-                     tr[TR_P_WAIT_MASK])) {  // wait for the rows to be resolved
-            ok = false;
-            break;
+      if (item == SI_K) {
+        const uint32_t n = st.nk++;
+        const int2 ci = cinfo[n % CD];
+        if (ci.x & CF_SEG_FIRST) {
+          if (tid == 0) {
+            if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
+              ok = false;
+            } else {
+              sas::mbar_arrive_expect_tx(&bars[B_QFULL], q_bytes);
+              for (int s = 0; s < NSLAB; ++s)
+                sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, ci.y);
+            }
           }
-          ok = load_chunk(cs, c0 + i < p.n_win_chunks);
+          ++seg_i;
         }
-        for (int i = 0; ok && i < nch; ++i) {  // V rows (the same rows again, mostly from L2)
-          ok = load_chunk((gch0 + i) % CD, c0 + i < p.n_win_chunks);
-          __syncwarp();
-          if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (gch0 + i) % CD]);
-        }
-        gchunk += nch;
+        if (ok) ok = load_chunk(n % CD, ci.x & CF_WIN);
+      } else {  // V rows: the K rows again, mostly from L2
+        const uint32_t n = st.nv++;
+        ok = load_chunk(n % CD, cinfo[n % CD].x & CF_WIN);
+        __syncwarp();
+        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);
       }
-      ++seg_i;
     }
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
@@ -1373,85 +1565,102 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_base = sas::smem_u32(smem + OFF_Q);
       const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
       const uint32_t p_base = sas::smem_u32(smem + OFF_P);
-      Walker wk;
-      wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
-      Seg sg;
-      uint32_t sc = 0, gp = 0, seg_i = 0;  // sc: ring slabs consumed so far, in the loaders' order
+      Stream st;
+      uint32_t sc = 0;               // ring slabs consumed so far, in the loaders' order
+      uint32_t kseg = 0, vseg = 0;   // segments begun by K, by V
       bool ok = true;
-      while (ok && wk.next(sg)) {
-        if (!twait(&bars[B_QFULL], seg_i & 1, abort_flag, p.status, 4, tracing, tr[TR_M_WAIT_Q])) break;
-        const int n_cmp = tokp[sg.t].n_cmp;
-        for (int k = sg.cb; ok && k < sg.ce; ++k) {
-          int c0, c1;
-          tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
-          const int nch = c1 - c0;
-          long long tg0 = 0;
-          // ---- S^T(i) = K(i) . Q^T
-          for (int i = 0; ok && i < nch; ++i) {
-            for (int s = 0; s < NSLAB; ++s, ++sc) {
-              const uint32_t slot = sc % kRing;
-              if (!twait(&bars[B_FULL + slot], (sc / kRing) & 1, abort_flag, p.status, 5, tracing,
-                         tr[TR_M_WAIT_FULL])) {
-                ok = false;
-                break;
-              }
-              sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
-              sas::tc_fence_after();
-              if (tracing && i == 0 && s == 0) tg0 = clock64();
+      while (ok) {
+        const int item = st.next<tracing>(bars, cinfo, abort_flag, p.status, tr[TR_M_WAIT_FULL]);
+        if (item == SI_END || item == SI_FAIL) break;
+        if (item == SI_K) {
+          // ---- S^T(n) = K(n) . Q^T into TMEM slot n % 4
+          const long long tq0 = tracing ? clock64() : 0;
+          const uint32_t n = st.nk++;
+          const int fl = cinfo[n % CD].x;
+          if (fl & CF_SEG_FIRST) {
+            if (!twait(&bars[B_QFULL], kseg & 1, abort_flag, p.status, 4, tracing, tr[TR_M_WAIT_Q])) break;
+            ++kseg;
+          }
+          // the slot's previous chunk n - 4 must have been read by its exp
+          // pass: implied by P.V(n - 4) if that was issued, else wait for P(n - 4)
+          if (n >= (uint32_t)kTileChunks && n - kTileChunks >= st.nv &&
+              !twait(&bars[B_PREADY2 + (n & 1)], ((n - kTileChunks) >> 1) & 1, abort_flag, p.status, 6, tracing,
+                     tr[TR_M_WAIT_P]))
+            break;
+          sas::tc_fence_after();
+          const uint32_t sd = TM_S + 64 * (n % kTileChunks);
+          for (int s = 0; s < NSLAB; ++s, ++sc) {
+            const uint32_t slot = sc % kRing;
+            if (!twait(&bars[B_FULL + slot], (sc / kRing) & 1, abort_flag, p.status, 5, tracing,
+                       tr[TR_M_WAIT_FULL])) {
+              ok = false;
+              break;
+            }
+            const long long tf0 = tracing ? clock64() : 0;
+            sas::fence_proxy_async_smem();  // cp.async (generic proxy) writes -> tensor-core reads
+            sas::tc_fence_after();
+            const long long tf1 = tracing ? clock64() : 0;
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 32, 16, 1024);
-                const uint64_t bd = sas::umma_desc_sw128(q_base + s * Q_SLAB_BYTES + kk * 32, 16, 1024);
-                sas::umma_ss(tmem + TM_S + 64 * i, ad, bd, idesc1, (s | kk) != 0);
-              }
-              sas::umma_commit(&bars[B_EMPTY + slot]);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 32, 16, 1024);
+              const uint64_t bd = sas::umma_desc_sw128(q_base + s * Q_SLAB_BYTES + kk * 32, 16, 1024);
+              sas::umma_ss(tmem + sd, ad, bd, idesc1, (s | kk) != 0);
+            }
+            sas::umma_commit(&bars[B_EMPTY + slot]);
+            if (tracing) {
+              tr[TR_S_SYNC1] += tf1 - tf0;
+              tr[TR_S_SYNC2] += clock64() - tf1;
             }
           }
           if (!ok) break;
-          sas::umma_commit(&bars[B_SFULL]);
-          if (k == sg.ce - 1) sas::umma_commit(&bars[B_QEMPTY]);
-          if (tracing) tr[TR_M_WAIT_O] += clock64() - tg0;
-          // ---- O^T += V^T(i) . P^T(i)
-          for (int i = 0; ok && i < nch; ++i) {
-            const bool first = k == sg.cb && i == 0;
-            if (!twait(&bars[B_PREADY2 + (gp & 1)], (gp >> 1) & 1, abort_flag, p.status, 6, tracing,
-                       tr[TR_M_WAIT_P])) {
-              ok = false;
+          sas::umma_commit(&bars[B_SF + n % kTileChunks]);
+          if (fl & CF_SEG_LAST) sas::umma_commit(&bars[B_QEMPTY]);
+          if (tracing) tr[TR_M_WAIT_O] += clock64() - tq0;  // QK^T section, waits included
+        } else {
+          // ---- O^T += V^T(n) . P^T(n)
+          const long long tv0 = tracing ? clock64() : 0;
+          const uint32_t n = st.nv++;
+          const int fl = cinfo[n % CD].x;
+          const bool first = fl & CF_SEG_FIRST;
+          if (!twait(&bars[B_PREADY2 + (n & 1)], (n >> 1) & 1, abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P]))
+            break;
+          if (first) {
+            if (vseg > 0 &&
+                !twait(&bars[B_OEMPTY], (vseg - 1) & 1, abort_flag, p.status, 7, tracing, tr[TR_M_WAIT_Q]))
               break;
-            }
-            if (first && seg_i > 0 &&
-                !twait(&bars[B_OEMPTY], (seg_i - 1) & 1, abort_flag, p.status, 7, tracing, tr[TR_M_WAIT_O])) {
-              ok = false;
-              break;
-            }
-            sas::tc_fence_after();
-            const uint32_t pb = p_base + (gp & 1) * P_BYTES;
-            for (int j = 0; j < 4; ++j, sc += 2) {
-              const uint32_t slot = sc % kRing;  // even: the pair (slot, slot + 1) never wraps
-              const uint32_t par = (sc / kRing) & 1;
-              if (!twait(&bars[B_FULL + slot], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL]) ||
-                  !twait(&bars[B_FULL + slot + 1], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL])) {
-                ok = false;
-                break;
-              }
-              sas::fence_proxy_async_smem();
-              sas::tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < 8; ++kk) {
-                const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 2048, SLAB_BYTES, 1024);
-                const uint64_t bd = sas::umma_desc_sw128(pb + kk * 2048, 8192, 1024);
-                sas::umma_ss(tmem + TM_O + 64 * j, ad, bd, idesc2, (first && kk == 0) ? 0u : 1u);
-              }
-              sas::umma_commit(&bars[B_EMPTY + slot]);
-              sas::umma_commit(&bars[B_EMPTY + slot + 1]);
-            }
-            if (!ok) break;
-            sas::umma_commit(&bars[B_PFREE + (gp & 1)]);
-            ++gp;
+            ++vseg;
           }
-          if (ok && k == sg.ce - 1) sas::umma_commit(&bars[B_OFULL]);
+          sas::tc_fence_after();
+          const uint32_t pb = p_base + (n & 1) * P_BYTES;
+          for (int j = 0; j < 4; ++j, sc += 2) {
+            const uint32_t slot = sc % kRing;  // even: the pair (slot, slot + 1) never wraps
+            const uint32_t par = (sc / kRing) & 1;
+            if (!twait(&bars[B_FULL + slot], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL]) ||
+                !twait(&bars[B_FULL + slot + 1], par, abort_flag, p.status, 12, tracing, tr[TR_M_WAIT_FULL])) {
+              ok = false;
+              break;
+            }
+            const long long tf0 = tracing ? clock64() : 0;
+            sas::fence_proxy_async_smem();
+            sas::tc_fence_after();
+            if (tracing) tr[TR_S_SYNC1] += clock64() - tf0;
+            const long long tf1 = tracing ? clock64() : 0;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint64_t ad = sas::umma_desc_sw128(kv_base + slot * SLAB_BYTES + kk * 2048, SLAB_BYTES, 1024);
+              const uint64_t bd = sas::umma_desc_sw128(pb + kk * 2048, 8192, 1024);
+              sas::umma_ss(tmem + TM_O + 64 * j, ad, bd, idesc2, (first && kk == 0) ? 0u : 1u);
+            }
+            sas::umma_commit(&bars[B_EMPTY + slot]);
+            sas::umma_commit(&bars[B_EMPTY + slot + 1]);
+            if (tracing) tr[TR_S_EXP] += clock64() - tf1;
+          }
+          if (!ok) break;
+          sas::umma_commit(&bars[B_PFREE + (n & 1)]);
+          if (fl & CF_SEG_LAST) sas::umma_commit(&bars[B_OFULL]);
+          sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);  // done with the chunk's flags
+          if (tracing) tr[TR_E_COPY] += clock64() - tv0;  // P.V section, waits included
         }
-        ++seg_i;
       }
     }
     __syncwarp();
@@ -1464,41 +1673,47 @@ __global__ void __launch_bounds__(kThreads, 1)
               GroupSync{&bars[half ? B_LSYNC : B_SSYNC], reinterpret_cast<uint32_t*>(misc + (half ? M_LWORD : M_SWORD)),
                         0},
               {}, tmem + ((uint32_t)(quad * 32) << 16), 0};
-    Walker wk;
-    wk.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
-    Seg sg;
-    uint32_t gchunk = 0, gtile = 0, gp = 0;
+    TileIter it;
+    it.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
+    Tile tl;
+    Seg pend{};         // a complete token whose output rows are still to be written
+    bool pending = false;
+    uint32_t gtile = 0, gp = 0;
     bool ok = true;
     const bool trace_me = tracing && half == 0;
     unsigned long long trb[TR_NSLOTS];
     unsigned long long* trp = half == 0 ? tr : trb;
-    while (ok && wk.next(sg)) {
-      const int n_cmp = tokp[sg.t].n_cmp;
-      for (int k = sg.cb; ok && k < sg.ce; ++k) {
-        int c0, c1;
-        tile_chunks(k, p.n_win_chunks, n_cmp, c0, c1);
-        const int nch = c1 - c0;
-        const uint32_t gch0 = gchunk;
-        for (int i = 0; ok && i < nch; ++i)  // the tile's validity masks
-          ok = twait(&bars[B_CFULL + (gch0 + i) % CD], ((gch0 + i) / CD) & 1, abort_flag, p.status, 8, trace_me,
-                     trp[TR_S_WAIT_MASK]);
-        float al;
-        int need;
-        if (ok)
-          ok = tile_max_pass<DT>(p, G, sm, bars, cmask, gtile, gch0, nch, k == sg.cb, g, al, need, abort_flag,
-                                 trace_me, trp);
-        for (int i = 0; ok && i < nch; ++i) {
-          ok = chunk_exp_pass<DT>(p, G, sm, bars, cmask, gch0 + i, i, i == 0 && need, k == sg.cb, al, gp,
-                                  abort_flag, trace_me, trp);
-          __syncwarp();
-          if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (gch0 + i) % CD]);
+    while (ok && it.next(tl, tokp, p.n_win_chunks)) {
+      for (int i = 0; ok && i < tl.nch; ++i)  // the tile's validity masks
+        ok = twait(&bars[B_CFULL + (tl.g0 + i) % CD], ((tl.g0 + i) / CD) & 1, abort_flag, p.status, 8, trace_me,
+                   trp[TR_S_WAIT_MASK]);
+      float al;
+      int need;
+      if (ok)
+        ok = tile_max_pass<DT>(p, G, sm, bars, cmask, gtile, tl.g0, tl.nch, tl.first, g, al, need, abort_flag,
+                               trace_me, trp);
+      for (int i = 0; ok && i < tl.nch; ++i) {
+        ok = chunk_exp_pass<DT>(p, G, sm, bars, cmask, tl.g0 + i, i, i == 0 && need, tl.first, al, gp, abort_flag,
+                                trace_me, trp);
+        __syncwarp();
+        if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (tl.g0 + i) % CD]);
+        if (ok && i == 0 && pending) {
+          ok = epilogue_second_half<DT>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
+          pending = false;
         }
-        gchunk += nch;
-        ++gtile;
-        if (ok && k == sg.ce - 1)
-          ok = segment_epilogue<DT>(p, G, sm, bars, sg, r, g, abort_flag, trace_me, trp);
+      }
+      ++gtile;
+      if (ok && tl.last) {
+        if (it.sg.complete) {
+          ok = epilogue_first_half<DT>(p, G, sm, it.sg, g, abort_flag);
+          pend = it.sg;
+          pending = true;
+        } else {
+          ok = segment_epilogue<DT>(p, G, sm, bars, it.sg, r, g, abort_flag, trace_me, trp);
+        }
       }
     }
+    if (ok && pending) ok = epilogue_second_half<DT>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
     if (FUSED && ok)
       zero_uncovered<DT>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
@@ -1518,6 +1733,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tp[TR_M_WAIT_P] = tr[TR_M_WAIT_P];
       tp[TR_M_WAIT_O] = tr[TR_M_WAIT_O];
       tp[TR_E_COPY] = tr[TR_E_COPY];
+      tp[TR_S_SYNC1] = tr[TR_S_SYNC1];  // MMA: async-proxy fences
+      tp[TR_S_SYNC2] = tr[TR_S_SYNC2];  // MMA: QK^T issue
+      tp[TR_S_EXP] = tr[TR_S_EXP];      // MMA: P.V issue
     } else if (tid == kSoftmaxWarp0 * 32) {
       tp[TR_S_WAIT_MASK] = tr[TR_S_WAIT_MASK];
       tp[TR_S_WAIT_S] = tr[TR_S_WAIT_S];
@@ -1532,7 +1750,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tp[TR_E_TMEM] = tr[TR_E_TMEM];
       tp[TR_E_STAGE] = tr[TR_E_STAGE];
       tp[TR_E_RED] = tr[TR_E_RED];
-      for (int i = TR_S_LD; i < TR_FIRST_S; ++i) tp[i] = tr[i];
+      for (int i = TR_S_LD; i < TR_FIRST_S; ++i)
+        if (i != TR_S_SYNC1 && i != TR_S_SYNC2 && i != TR_S_EXP) tp[i] = tr[i];
     }
   }
   sas::tc_fence_before();

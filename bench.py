@@ -560,7 +560,9 @@ def ours_arm(a, rank, world, local_rank):
     if a.config == "C4":
         line["roofline"].update({"bound": "tensor", "unit": "TFLOP/s",
                                  "achieved": work["flops"] / (attn_ms * 1e-3) / 1e12,
-                                 "peak": peaks.get("bf16_tflops", 1590.0)})
+                                 "peak": peaks.get("bf16_tflops", 1590.0),
+                                 "peak_source": ("measured (MEASURED_PEAKS.json bf16_tflops, burst: clocks stay at "
+                                                 "max over the timed steps)") if peaks else "fallback"})
         line["roofline"]["frac"] = line["roofline"]["achieved"] / line["roofline"]["peak"]
     if world == 1 and not a.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(dict(d, q=q), H, K, a.cpu_seconds)

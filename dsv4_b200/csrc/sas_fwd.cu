@@ -88,11 +88,12 @@ constexpr float kLn2 = 0.6931471805599453f;
 // every chunk starts on an even slab number, so the slab pair (2j, 2j+1) of
 // P.V's d-tile j always sits in two adjacent slots (fixed operand stride).
 constexpr int kRing = 6;
+constexpr int kPBuf = 2;                                   // P^T buffers: chunk n uses buffer n % kPBuf
 constexpr int P_BYTES = CH * 128;                         // one P^T buffer, 16 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = OFF_Q + NSLAB * Q_SLAB_BYTES;     // 64 KB
 constexpr int OFF_P = OFF_KV + kRing * SLAB_BYTES;       // +96 KB
-constexpr int OFF_MISC = OFF_P + 2 * P_BYTES;            // +32 KB (double-buffered P^T)
+constexpr int OFF_MISC = OFF_P + kPBuf * P_BYTES;
 // misc region
 constexpr int M_BAR = 0;         // 48 mbarriers x 8 B
 constexpr int M_TMEM = 384;      // tmem base address
@@ -138,6 +139,9 @@ constexpr int B_CEMPTY = 36;     // CD: slot done with by the loader warps, the 
 constexpr int B_SF = 44;         // kTileChunks: S^T of chunk n landed in TMEM slot n % kTileChunks
 static_assert(B_CFULL + CD <= B_LSYNC && B_CEMPTY + CD <= B_SF && B_SF + kTileChunks <= 48, "barrier map");
 constexpr int kCemptyCount = kLoaderWarps + 8 + 1;  // loader warps + softmax warps + the MMA thread
+// P^T buffer of chunk n, and the phase parity of that buffer's barriers for it
+__device__ __forceinline__ uint32_t pbuf(uint32_t n) { return n % kPBuf; }
+__device__ __forceinline__ uint32_t pphase(uint32_t n) { return (n / kPBuf) & 1; }
 
 // Per-chunk flags published by the coordinate warp with the chunk's rows
 // (int2 {flags, token} per coordinate-ring slot).
@@ -803,15 +807,13 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
 #pragma unroll
     for (int h = 0; h < 32; ++h) x[h] = valid ? sas::ex2(__uint_as_float(ra[h]) * p.scale_log2 - mw[h]) : 0.f;
   }
-  // P buffer gp % 2 is free once P.V of chunk gp - 2 is done (phase
-  // (gp - 2) / 2 of that buffer's barrier); a rescale of O^T also needs
-  // P.V of chunk gp - 1 done
-  if (gp > 1 && !twait(&bars[B_PFREE + (gp & 1)], ((gp - 2) >> 1) & 1, abort_flag, p.status, 13, tracing,
-                       tr[TR_S_WAIT_O]))
+  // P buffer pbuf(gp) is free once P.V of chunk gp - kPBuf is done; a
+  // rescale of O^T also needs P.V of chunk gp - 1 done
+  if (gp >= (uint32_t)kPBuf && !twait(&bars[B_PFREE + pbuf(gp - kPBuf)], pphase(gp - kPBuf), abort_flag, p.status,
+                                      13, tracing, tr[TR_S_WAIT_O]))
     return false;
-  if (rescale_now && gp > 0 &&
-      !twait(&bars[B_PFREE + ((gp - 1) & 1)], ((gp - 1) >> 1) & 1, abort_flag, p.status, 13, tracing,
-             tr[TR_S_WAIT_O]))
+  if (kPBuf > 1 && rescale_now && gp > 0 &&
+      !twait(&bars[B_PFREE + pbuf(gp - 1)], pphase(gp - 1), abort_flag, p.status, 13, tracing, tr[TR_S_WAIT_O]))
     return false;
   sas::tc_fence_after();
   if (rescale_now) {
@@ -833,7 +835,7 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
   }
 #pragma unroll
   for (int h = 0; h < 32; ++h) G.lsum[h] += x[h];
-  uint8_t* prow = S.pbuf + (gp & 1) * P_BYTES + G.gst * 128;
+  uint8_t* prow = S.pbuf + pbuf(gp) * P_BYTES + G.gst * 128;
 #pragma unroll
   for (int c4 = 0; c4 < 4; ++c4) {
     const int cc = (G.hb >> 3) + c4;  // 16-byte column chunk of the 128-byte row
@@ -844,7 +846,7 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
   }
   sas::fence_proxy_async_smem();
   sas::tc_fence_before();
-  sas::mbar_arrive(&bars[B_PREADY2 + (gp & 1)]);
+  sas::mbar_arrive(&bars[B_PREADY2 + pbuf(gp)]);
   ++gp;
   if (tracing) {
     tr[TR_S_SOFTMAX] += clock64() - ts0;
@@ -1308,7 +1310,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kTileChunks; ++i) sas::mbar_init(&bars[B_SF + i], 1);
     sas::mbar_init(&bars[B_OFULL], 1);
     sas::mbar_init(&bars[B_OEMPTY], 256);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kPBuf; ++i) {
       sas::mbar_init(&bars[B_PREADY2 + i], 256);
       sas::mbar_init(&bars[B_PFREE + i], 1);
     }
@@ -1356,6 +1358,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
   for (int i = 0; i < TR_NSLOTS; ++i) tr[i] = 0;
   const long long t_start = tracing ? clock64() : 0;
+  // event timeline of the CTA's first chunks (trace builds only): slot i of
+  // 16 per CTA after the counters, SM cycles since kernel entry
+  auto ev = [&](int i) {
+    if (TRACE) p.trace[(size_t)gridDim.x * TR_NSLOTS + (size_t)blockIdx.x * 16 + i] = clock64() - t_entry;
+  };
+  if (TRACE && tid == 0) ev(15);
 
   if (warp == kCoordWarp) {
     // =============================== row resolution, up to CD chunks ahead
@@ -1444,6 +1452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
       }
       if (tracing) tr[TR_P_COORD] += clock64() - tc0;
+      if (TRACE && lane == 0 && tl.g0 == 0) ev(0);
+      if (TRACE && lane == 0 && tl.g0 > 0 && tl.g0 <= (uint32_t)kTileChunks && !tl.first) ev(2);
 #pragma unroll
       for (int j = 0; j < kTileChunks; ++j) {
         if (j >= tl.nch) break;
@@ -1467,6 +1477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) sas::mbar_arrive(&bars[B_CFULL + slot]);
+        if (TRACE && lane == 0 && gc == 0) ev(1);
+        if (TRACE && lane == 0 && gc == 4) ev(3);
         // start the chunk's rows on their way into L2 for the loaders
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -1548,9 +1560,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++seg_i;
         }
         if (ok) ok = load_chunk(n % CD, ci.x & CF_WIN);
+        if (TRACE && tid == 0 && n == 0) ev(5);
+        if (TRACE && tid == 0 && n == 4) ev(6);
       } else {  // V rows: the K rows again, mostly from L2
         const uint32_t n = st.nv++;
         ok = load_chunk(n % CD, cinfo[n % CD].x & CF_WIN);
+        if (TRACE && tid == 0 && n == 0) ev(4);
         __syncwarp();
         if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);
       }
@@ -1584,7 +1599,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // the slot's previous chunk n - 4 must have been read by its exp
           // pass: implied by P.V(n - 4) if that was issued, else wait for P(n - 4)
           if (n >= (uint32_t)kTileChunks && n - kTileChunks >= st.nv &&
-              !twait(&bars[B_PREADY2 + (n & 1)], ((n - kTileChunks) >> 1) & 1, abort_flag, p.status, 6, tracing,
+              !twait(&bars[B_PREADY2 + pbuf(n - kTileChunks)], pphase(n - kTileChunks), abort_flag, p.status, 6, tracing,
                      tr[TR_M_WAIT_P]))
             break;
           sas::tc_fence_after();
@@ -1615,6 +1630,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           sas::umma_commit(&bars[B_SF + n % kTileChunks]);
           if (fl & CF_SEG_LAST) sas::umma_commit(&bars[B_QEMPTY]);
+          if (TRACE && n == 0) ev(7);
+          if (TRACE && n == 4) ev(8);
           if (tracing) tr[TR_M_WAIT_O] += clock64() - tq0;  // QK^T section, waits included
         } else {
           // ---- O^T += V^T(n) . P^T(n)
@@ -1622,7 +1639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t n = st.nv++;
           const int fl = cinfo[n % CD].x;
           const bool first = fl & CF_SEG_FIRST;
-          if (!twait(&bars[B_PREADY2 + (n & 1)], (n >> 1) & 1, abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P]))
+          if (!twait(&bars[B_PREADY2 + pbuf(n)], pphase(n), abort_flag, p.status, 6, tracing, tr[TR_M_WAIT_P]))
             break;
           if (first) {
             if (vseg > 0 &&
@@ -1631,7 +1648,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ++vseg;
           }
           sas::tc_fence_after();
-          const uint32_t pb = p_base + (n & 1) * P_BYTES;
+          const uint32_t pb = p_base + pbuf(n) * P_BYTES;
           for (int j = 0; j < 4; ++j, sc += 2) {
             const uint32_t slot = sc % kRing;  // even: the pair (slot, slot + 1) never wraps
             const uint32_t par = (sc / kRing) & 1;
@@ -1656,9 +1673,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (tracing) tr[TR_S_EXP] += clock64() - tf1;
           }
           if (!ok) break;
-          sas::umma_commit(&bars[B_PFREE + (n & 1)]);
+          sas::umma_commit(&bars[B_PFREE + pbuf(n)]);
           if (fl & CF_SEG_LAST) sas::umma_commit(&bars[B_OFULL]);
           sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);  // done with the chunk's flags
+          if (TRACE && n == 0) ev(9);
+          if (TRACE && n == 4) ev(10);
           if (tracing) tr[TR_E_COPY] += clock64() - tv0;  // P.V section, waits included
         }
       }
@@ -1692,6 +1711,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok)
         ok = tile_max_pass<DT>(p, G, sm, bars, cmask, gtile, tl.g0, tl.nch, tl.first, g, al, need, abort_flag,
                                trace_me, trp);
+      if (TRACE && tid == kSoftmaxWarp0 * 32 && gtile < 2) ev(11 + gtile);
       for (int i = 0; ok && i < tl.nch; ++i) {
         ok = chunk_exp_pass<DT>(p, G, sm, bars, cmask, tl.g0 + i, i, i == 0 && need, tl.first, al, gp, abort_flag,
                                 trace_me, trp);
@@ -1713,7 +1733,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+    if (TRACE && tid == kSoftmaxWarp0 * 32) ev(13);
     if (ok && pending) ok = epilogue_second_half<DT>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
+    if (TRACE && tid == kSoftmaxWarp0 * 32) ev(14);
     if (FUSED && ok)
       zero_uncovered<DT>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);

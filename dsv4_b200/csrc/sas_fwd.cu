@@ -7,39 +7,45 @@
 //    linearised (b, s) ids exactly like the reference kernel's outer loop
 //    (kernel.py:254-278: pid in [bn2_start*max_seq+m_start,
 //    bn2_end*max_seq+m_end), s < act_q), and gives every covered query token
-//    its work in 128-row chunks: ceil((win_left+1)/128) window chunks plus
-//    ceil(n_cmp/128) compressed chunks, n_cmp = min(K, threshold) for SCFA,
-//    threshold for CFA (threshold = (s_g+1)//ratio, golden.py:41-51).
-//    An exclusive scan gives each token's first chunk-unit. Output rows of
+//    its work in tiles: the window tile(s) plus ceil(n_cmp/512) compressed
+//    tiles, n_cmp = min(K, threshold) for SCFA, threshold for CFA
+//    (threshold = (s_g+1)//ratio, golden.py:41-51).
+//    An exclusive scan gives each token's first unit. Output rows of
 //    tokens without work are zeroed (golden.py leaves them zero), and the
 //    split-token arrival counters are cleared.
 //
 // 2. sas_fwd_kernel (persistent, R x G CTAs, one per SM): the unit sequence
-//    is cut into R equal contiguous ranges; the G CTAs of a range each own
-//    64 query heads (head group g) and walk the same rows, so the second
-//    reader of every KV row hits L2. Per CTA, warp-specialised:
-//      warps 0-3 loaders: one KV row per thread; resolve window positions /
-//               top-k ids through the block tables (kernel.py:285-401,
-//               686-766), publish a 128-bit row-validity mask, and gather the
-//               128 rows x 512 cols chunk with 16-byte cp.async into eight
-//               64-col slabs in the 128B-swizzled K-major layout (masked rows
-//               are zero-filled without a read).
-//      warp 8   MMA issuer (one thread) and TMEM owner: transposed attention
+//    (one unit = one softmax tile of a token: the window rows, then the
+//    compressed rows in tiles of 512, as golden.py tiles them) is cut into R
+//    contiguous ranges; the G CTAs of a range each own 64 query heads (head
+//    group g) and walk the same rows, so the second reader of every KV row
+//    hits L2. A tile's running-max update uses that tile's exact max, so P is
+//    rounded at the same points as the reference; since the max needs every
+//    score of the tile first, each 128-row chunk is copied twice: K(n) for
+//    the scores, then V(n) (the same rows, mostly from L2) for P.V.
+//    Per CTA, warp-specialised (12 warps):
+//      warp 3   rows: resolves window positions / top-k ids through the
+//               block tables (kernel.py:285-401, 686-766) a tile at a time,
+//               and publishes per chunk the pool rows, a 128-bit validity
+//               mask and the chunk's flags into an 8-deep ring.
+//      warps 0-1 loaders: 16-byte cp.async of the rows into 16 KB slabs
+//               (128B-swizzled K-major; masked rows zero-filled without a
+//               read), in the copy-stream order shared with the MMA thread.
+//      warp 2   MMA issuer (one thread) and TMEM owner: transposed attention
 //               so the KV rows fill the M=128 datapath and the 64 heads are N:
 //                 S^T[128 x 64]  = K[128 x 512] . Q^T          (K-major A and B)
 //                 O^T[512 x 64] += V^T[512 x 128] . P^T[128 x 64] (4 MMAs of
-//               M=128; V^T is the SAME smem tile read MN-major, since K=V)
-//               TMEM: S^T in cols [0,64), O^T tiles in cols [64,320).
-//      warps 4-7 softmax / epilogue: one thread per KV row (TMEM lane). The
-//               row mask (window idx <= s_g; compressed 0 <= idx < threshold,
-//               scan stopped at the first -1) sets scores to -inf; per-head
-//               maxima are warp redux.max plus a 4-way smem merge; the state
-//               starts at (m, l) = (sink, 1) in log2 units (kernel.py:594-618,
-//               golden.py:156-160) and O^T is only rescaled when a head's max
-//               grows by more than 2^8. P is rounded to the I/O dtype before
-//               P.V while l sums the unrounded p (golden.py:191-195).
-//               Epilogue: O/l, lse = m + ln l.
-//    A token whose chunks all fall in one range is finished in place (sink
+//               M=128; V^T is the slab pair read MN-major, since K=V)
+//               TMEM: 4 score slots in cols [0,256), O^T in cols [256,512).
+//      warps 4-11 softmax / epilogue, two groups of 32 heads: one thread per
+//               KV row (TMEM lane). The row mask (window idx <= s_g;
+//               compressed 0 <= idx < threshold, scan stopped at the first
+//               -1) sets scores to -inf; per-head maxima are warp redux.max
+//               plus a 4-way smem merge; the state starts at (m, l) =
+//               (sink, 1) in log2 units (kernel.py:594-618, golden.py:156-160).
+//               P is rounded to the I/O dtype before P.V while l sums the
+//               unrounded p (golden.py:191-195). Epilogue: O/l, lse = m + ln l.
+//    A token whose tiles all fall in one range is finished in place (sink
 //    folded in). A token cut by range boundaries leaves normalised partials
 //    (o, lse2) in the workspace; the CTA that lands the token's last partial
 //    merges them: lse = log2(sum 2^lse_i + 2^sink), out = sum 2^(lse_i-lse) o_i.

@@ -69,7 +69,7 @@ constexpr int Q_SLAB_BYTES = HG * 128;  // 8 KB
 constexpr int kLoaderWarps = 2;         // warps 0-1: cp.async copies of K and V rows
 constexpr int kLoaderThreads = 32 * kLoaderWarps;
 constexpr int kMmaWarp = 2;             // warp 2: TMEM owner and MMA issuer
-constexpr int kCoordWarp = 3;           // warp 3: row resolution + L2 prefetch, runs ahead
+constexpr int kCoordWarp = 3;           // warp 3: row resolution, runs up to two tiles ahead
 constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax group A (heads 0-31) / epilogue
 constexpr int kSoftmaxWarpB = 8;        // warps 8-11: softmax group B (heads 32-63) / epilogue
 constexpr int kThreads = 32 * 12;
@@ -1401,7 +1401,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       const bool is_win = tl.c0 < p.n_win_chunks;  // a tile is all window or all compressed
-      const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
       int coord[kTileChunks][4];
       bool val[kTileChunks][4];
       if (is_win) {
@@ -1485,14 +1484,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) sas::mbar_arrive(&bars[B_CFULL + slot]);
         if (TRACE && lane == 0 && gc == 0) ev(1);
         if (TRACE && lane == 0 && gc == 4) ev(3);
-        // start the chunk's rows on their way into L2 for the loaders
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          if (val[j][k]) {
-            const uint8_t* rp = pool + (size_t)coord[j][k] * (D * 2);
-#pragma unroll
-            for (int l = 0; l < 8; ++l) sas::prefetch_l2_line(rp + l * 128);
-          }
       }
     }
     if (ok) {  // the end of the stream, as one more ring slot

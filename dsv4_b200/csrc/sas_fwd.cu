@@ -75,10 +75,6 @@ constexpr int kSoftmaxWarpB = 8;        // warps 8-11: softmax group B (heads 32
 constexpr int kThreads = 32 * 12;
 constexpr int kTileChunksC = 4;          // chunks per softmax tile (512 rows)
 constexpr int CD = 2 * kTileChunksC;     // depth of the row-coordinate ring (chunks): two tiles
-// Chunks a token may hold beyond a range's length before it is cut across
-// ranges: a cut costs the partial write-back and the merge, about this many
-// chunks of work.
-constexpr int kCutCost = 1;  // in units (tiles)
 // A unit of work is one softmax tile of a token, as golden.py tiles the KV
 // (GOLDEN_S2_TILE = 512 rows): the window rows, then the compressed rows in
 // tiles of 512, i.e. up to kTileChunks 128-row chunks. The running max is
@@ -202,6 +198,7 @@ struct FwdParams {
   int32_t* status;
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
+  int cut_cost;              // split tokens longer than a range plus this many tiles (< 0: never)
   // fused plan (T <= kFusedMaxT): the CTA builds the token plan itself and
   // checks metadata coverage at output time
   int fused, early;          // early: the preceding kernel is our metadata kernel
@@ -380,17 +377,19 @@ __device__ __forceinline__ int warp_last_le(const int32_t* us, int T, int x, int
   return lo;
 }
 
-
 // First unit of range r: r*u, moved back to the start of the token holding
-// it unless that token is too long to keep whole (more than u + kCutCost
-// units). Boundaries inside a cut token are therefore always r*u exactly.
-__device__ __forceinline__ int range_start(const int32_t* us, int T, int U, int u, int r, int lane) {
+// it unless splitting is enabled (cut_cost >= 0) and the token holds more
+// than a range plus cut_cost tiles; boundaries inside a split token are
+// therefore always r*u exactly. By default tokens are never split: the
+// reference keeps every token on one core, and a piece that starts a token's
+// softmax from the sink rounds P against its own running max, not the token's.
+__device__ __forceinline__ int range_start(const int32_t* us, int T, int U, int u, int r, int lane, int cut_cost) {
   if (r <= 0) return 0;
   const long long x = (long long)r * u;
   if (x >= U) return U;
   const int t = warp_last_le(us, T, (int)x, lane);
   const int st = us[t], n = us[t + 1] - st;
-  return (x == st || n > u + kCutCost) ? (int)x : st;
+  return (x == st || (cut_cost >= 0 && n > u + cut_cost)) ? (int)x : st;
 }
 
 // A CTA's unit range [u0, end) and the token holding u0, computed once per
@@ -399,12 +398,12 @@ struct RangeInfo {
   int u0, end, t, u;
 };
 
-__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, int T, int R, int r, int lane) {
+__device__ __forceinline__ RangeInfo compute_range(const int32_t* us, int T, int R, int r, int lane, int cut_cost) {
   RangeInfo ri;
   const int U = us[T];
   ri.u = (U + R - 1) / R;
-  ri.u0 = range_start(us, T, U, ri.u, r, lane);
-  ri.end = r + 1 >= R ? U : range_start(us, T, U, ri.u, r + 1, lane);
+  ri.u0 = range_start(us, T, U, ri.u, r, lane, cut_cost);
+  ri.end = r + 1 >= R ? U : range_start(us, T, U, ri.u, r + 1, lane, cut_cost);
   ri.t = ri.u0 < U ? warp_last_le(us, T, ri.u0, lane) : T - 1;
   return ri;
 }
@@ -1351,7 +1350,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fused_plan<DT>(p, s_tok, s_us,
                    reinterpret_cast<int*>(smem + OFF_PLAN + P_SMAX), reinterpret_cast<int*>(red));
   if (warp == 0) {
-    const RangeInfo ri = compute_range(usp, p.T, p.R, r, lane);
+    const RangeInfo ri = compute_range(usp, p.T, p.R, r, lane, p.cut_cost);
     if (lane == 0) *reinterpret_cast<RangeInfo*>(misc + M_RANGE) = ri;
   }
   if (tid == 32) sas::tma_prefetch_desc(&tm_q);
@@ -1834,6 +1833,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 // Tuning / diagnostics knobs set through sas_fwd_set_option (process-wide).
 float g_tau = 0.0f;  // exact running max (golden.py); > 0 only for experiments
+int g_cut_cost = -1; // tokens are never split across CTAs unless set
 unsigned long long* g_trace = nullptr;
 
 struct WsLayout {
@@ -1864,6 +1864,10 @@ extern "C" int sas_fwd_set_option(int32_t option, double value, void* ptr) {
       return SAS_OK;
     case SAS_OPT_TRACE_BUFFER:
       g_trace = static_cast<unsigned long long*>(ptr);
+      return SAS_OK;
+    case SAS_OPT_SPLIT_TOKENS:
+      if (!(value >= -1.0 && value <= 1e6)) return SAS_ERR_INVALID_ARG;
+      g_cut_cost = value < 0.0 ? -1 : (int)value;
       return SAS_OK;
     default:
       return SAS_ERR_INVALID_ARG;
@@ -1987,6 +1991,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.status = status;
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;
+  fp.cut_cost = g_cut_cost;
   fp.fused = fused ? 1 : 0;
   fp.early = early ? 1 : 0;
   fp.B = batch;

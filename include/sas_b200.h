@@ -158,14 +158,24 @@ int sas_sparse_attn_sharedkv_fwd(
  * Process-wide options of the forward kernel (no counterpart in the
  * reference, whose knobs are compile-time JIT parameters, api.py:59-126).
  *   SAS_OPT_RESCALE_THRESHOLD (value): the online softmax keeps a per-head
- *     running max m and only rescales the accumulator when a new chunk's max
- *     exceeds m by more than `value` (log2 units; default 8, 0 = rescale on
- *     every increase, like the reference kernel's per-chunk update).
- *   SAS_OPT_TRACE_BUFFER (ptr): device buffer of 16 uint64 per CTA that
- *     receives per-role cycle counters of the next launches (NULL = off).
+ *     running max m, raised once per 512-row tile with the tile's exact max,
+ *     so P is rounded at the same points as golden.py. With value > 0 the max
+ *     (and the accumulator) is only moved when a tile's max exceeds m by more
+ *     than `value` (log2 units). Default 0: exact.
+ *   SAS_OPT_TRACE_BUFFER (ptr): device buffer of 46 uint64 per CTA (30 per-role
+ *     cycle counters for every CTA, then 16 event timestamps per CTA) that
+ *     receives the diagnostics of the next launches (NULL = off).
+ *   SAS_OPT_SPLIT_TOKENS (value): by default a token is never split across
+ *     CTAs, as the reference keeps every token on one core. With value >= 0, a
+ *     token longer than a range plus `value` tiles is split at range
+ *     boundaries and its pieces are merged in fp32 (split-KV). Faster for a
+ *     few very long tokens, but a piece other than the first rounds P against
+ *     its own running max, so such tokens meet the accuracy bounds and not the
+ *     reference's rounding points. value < 0 restores the default.
  * ---------------------------------------------------------------------- */
 #define SAS_OPT_RESCALE_THRESHOLD 1
 #define SAS_OPT_TRACE_BUFFER 2
+#define SAS_OPT_SPLIT_TOKENS 3
 int sas_fwd_set_option(int32_t option, double value, void* ptr);
 
 #ifdef __cplusplus

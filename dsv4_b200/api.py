@@ -88,8 +88,6 @@ def sparse_attn_sharedkv(
     assert layout_kv == "PA_ND", "only layout_kv=PA_ND supported"
     assert layout_q in ("TND", "BSND"), f"unsupported layout_q={layout_q!r}"
     dcode = _dtype_code(q.dtype)
-    if not q.is_cuda:
-        raise RuntimeError("sparse_attn_sharedkv needs q on a CUDA device (no CPU path)")
     dev = q.device
 
     if cmp_kv is None:
@@ -132,6 +130,12 @@ def sparse_attn_sharedkv(
         idx_dev = None
     if N2 != 1 or D != 512 or N1 % 8 != 0 or N1 <= 0:
         raise ValueError(f"only N2=1, D=512 and N1 a multiple of 8 supported (got N1={N1}, N2={N2}, D={D})")
+    if metadata is not None:
+        assert metadata.numel() == SAS_META_SIZE, \
+            f"metadata must have {SAS_META_SIZE} int32 entries (got {metadata.numel()})"
+    # every host-side check above runs before the device is needed
+    if not q.is_cuda:
+        raise RuntimeError("sparse_attn_sharedkv needs q on a CUDA device (no CPU path)")
     cmp_ratio_eff = cmp_ratio if cmp_ratio is not None else 4
 
     ori_kv_dev = ori_kv.to(dev).contiguous()

@@ -61,23 +61,47 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait. `abort_flag` is a CTA-shared word raised by whichever role
-// first gives up, so the others stop waiting for work that will not come.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int where) {
+// CTA-shared control block of the bounded waits: `abort` is raised by
+// whichever role first gives up, so the others stop waiting for work that will
+// not come; `limit_ns` is the launch's wait limit (SAS_WAIT_LIMIT_NS unless the
+// caller set another one).
+struct CtaCtl {
+  int abort;
+  int pad;
+  unsigned long long limit_ns;
+};
+
+// Bounded wait. Returns false when the CTA is aborting or the limit ran out;
+// in the latter case status records SAS_ERR_TIMEOUT_BASE + where.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile CtaCtl* ctl, int* status,
+                                          int where) {
   if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer();
+  const uint64_t lim = ctl->limit_ns;
   uint32_t n = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > SAS_WAIT_LIMIT_NS) {
-        *abort_flag = 1;
+      if (ctl->abort) return false;
+      if (globaltimer() - t0 > lim) {
+        ctl->abort = 1;
         if (status) atomicCAS(status, 0, SAS_ERR_TIMEOUT_BASE + where);
         return false;
       }
     }
+  }
+}
+
+// Bounded wait that does not give up when the CTA aborts: used to drain
+// asynchronous work (MMAs, bulk copies) that is already in flight before the
+// CTA frees the resources it targets. Always finite (limit_ns).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer() - t0 > limit_ns) return false;
   }
 }
 
@@ -247,6 +271,10 @@ __host__ __device__ __forceinline__ int64_t floordiv64(int64_t a, int64_t b) {
 // Make the device that owns `ptr` current for this runtime instance. The
 // library links the CUDA runtime statically, so its notion of the current
 // device is separate from the caller's; every entry point calls this first.
+// Row-scan cap of the scheduler's greedy walk (SAS_OPT_SCHED_SCAN_CAP;
+// <= 0 restores the default), defined with the scheduler.
+void set_sched_scan_cap(long long cap);
+
 inline bool select_device_of(const void* ptr) {
   cudaPointerAttributes a;
   if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {

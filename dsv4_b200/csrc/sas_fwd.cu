@@ -99,9 +99,9 @@ constexpr int OFF_MISC = OFF_P + kPBuf * P_BYTES;
 // misc region
 constexpr int M_BAR = 0;         // 48 mbarriers x 8 B
 constexpr int M_TMEM = 384;      // tmem base address
-constexpr int M_ABORT = 388;
-constexpr int M_LWORD = 400;     // 3 words: group B (softmax warps 8-11) OR
-constexpr int M_SWORD = 416;     // 3 words: group A (softmax warps 4-7) OR
+constexpr int M_ABORT = 392;     // sas::CtaCtl (abort flag, wait limit), 16 B
+constexpr int M_LWORD = 408;     // 3 words: group B (softmax warps 8-11) OR
+constexpr int M_SWORD = 420;     // 3 words: group A (softmax warps 4-7) OR
 constexpr int M_RANGE = 432;     // RangeInfo of this CTA (4 ints)
 constexpr int M_CMASK = 448;     // CD x 4 words: row-validity mask per ring slot
 constexpr int M_RED = M_CMASK + CD * 16;  // [2 tile parities][4 quads][64 heads] per-warp maxima, 2 KB
@@ -128,6 +128,7 @@ constexpr int B_FULL = 0;        // kRing
 constexpr int B_EMPTY = 8;       // kRing
 constexpr int B_QFULL = 16;
 constexpr int B_QEMPTY = 17;
+constexpr int B_DRAIN = 18;      // the MMA thread's final commit: every tcgen05.mma it issued is done
 constexpr int B_OFULL = 20;
 constexpr int B_OEMPTY = 21;
 // Per P^T buffer b (chunk n uses buffer n % 2), so that each completes once per
@@ -180,7 +181,7 @@ struct PlanParams {
 struct FwdParams {
   int T, H, G, R, scenario, K, ratio, win_left, n_win_chunks;
   int ori_bs, ori_bt_stride, cmp_bs, cmp_bt_stride;
-  int ori_rows, cmp_rows;  // OOB row coordinate = row count
+  int ori_nblk, cmp_nblk;  // pool sizes in blocks: table entries outside [0, nblk) are dropped and flagged
   const uint8_t* ori_kv;   // paged pools, rows of D elements
   const uint8_t* cmp_kv;
   const int32_t* ori_bt;
@@ -199,6 +200,7 @@ struct FwdParams {
   int q_box_h;
   float tau;                 // lazy-rescale threshold, log2 units (0 = exact running max)
   int cut_cost;              // split tokens longer than a range plus this many tiles (< 0: never)
+  unsigned long long wait_ns;  // limit of every bounded wait
   // fused plan (T <= kFusedMaxT): the CTA builds the token plan itself and
   // checks metadata coverage at output time
   int fused, early;          // early: the preceding kernel is our metadata kernel
@@ -532,7 +534,7 @@ __device__ __forceinline__ void warp_reduce_scatter(float (&v)[N], int lane) {
   }
 }
 
-__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status,
+__device__ __forceinline__ bool twait(uint64_t* bar, uint32_t parity, volatile sas::CtaCtl* abort_flag, int* status,
                                       int where, bool tracing, unsigned long long& acc) {
   const long long t0 = tracing ? clock64() : 0;
   const bool r = sas::mbar_wait(bar, parity, abort_flag, status, where);
@@ -556,7 +558,7 @@ struct Stream {
   uint32_t nk = 0, nv = 0;  // next chunk for K, for V
   bool kend = false;        // every chunk has had its K
   template <bool TR>
-  __device__ __forceinline__ int next(uint64_t* bars, const int2* cinfo, volatile int* abort_flag, int* status,
+  __device__ __forceinline__ int next(uint64_t* bars, const int2* cinfo, volatile sas::CtaCtl* abort_flag, int* status,
                                       unsigned long long& tslot) {
     if (!kend && nk <= nv + kTileChunks) {
       if (!twait(&bars[B_CFULL + nk % CD], (nk / CD) & 1, abort_flag, status, 3, TR, tslot)) return SI_FAIL;
@@ -582,7 +584,7 @@ struct GroupSync {
   uint64_t* bar;
   uint32_t* words;
   uint32_t ph;
-  __device__ __forceinline__ bool sync_or(int pred, int lane, bool lead, int& result, volatile int* abort_flag,
+  __device__ __forceinline__ bool sync_or(int pred, int lane, bool lead, int& result, volatile sas::CtaCtl* abort_flag,
                                           int* status, int where) {
     const bool any = __any_sync(0xffffffffu, pred);
     __syncwarp();
@@ -597,7 +599,7 @@ struct GroupSync {
     ++ph;
     return ok;
   }
-  __device__ __forceinline__ bool sync(int lane, bool lead, volatile int* abort_flag, int* status, int where) {
+  __device__ __forceinline__ bool sync(int lane, bool lead, volatile sas::CtaCtl* abort_flag, int* status, int where) {
     int unused;
     return sync_or(0, lane, lead, unused, abort_flag, status, where);
   }
@@ -664,7 +666,7 @@ __device__ __forceinline__ size_t part_slot(const FwdParams& p, int rr, int r0, 
 
 template <int DT>
 __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g, int r0, int r1, int wf,
-                                                SmGroup& G, float* lse_s, volatile int* abort_flag) {
+                                                SmGroup& G, float* lse_s, volatile sas::CtaCtl* abort_flag) {
   using IO = IoType<DT>;
   const int ns = r1 - r0 + 1;
   const int hn = min(HG, p.H - g * HG);  // heads of this group
@@ -735,7 +737,7 @@ template <int DT>
 __device__ __forceinline__ bool tile_max_pass(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
                                               const uint32_t* cmask, uint32_t gtile, uint32_t gch0, int nch,
                                               bool first_tile_of_seg, int g, float& al, int& need,
-                                              volatile int* abort_flag, bool tracing, unsigned long long* tr) {
+                                              volatile sas::CtaCtl* abort_flag, bool tracing, unsigned long long* tr) {
   float* mw = warp_mrun(S, G);
   if (first_tile_of_seg) {
     const int h = g * HG + G.hb + G.lane;
@@ -799,7 +801,7 @@ template <int DT>
 __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
                                                const uint32_t* cmask, uint32_t gchunk, int i, bool rescale_now,
                                                bool first_tile_of_seg, float al, uint32_t& gp,
-                                               volatile int* abort_flag, bool tracing, unsigned long long* tr) {
+                                               volatile sas::CtaCtl* abort_flag, bool tracing, unsigned long long* tr) {
   using IO = IoType<DT>;
   const long long ts0 = tracing ? clock64() : 0;
   const float* mw = warp_mrun(S, G);
@@ -869,7 +871,7 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
 template <int DT>
 __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, const SmShared& S, float* mw,
                                                 int t, int g, int r0, int r1, int wf, int own_r,
-                                                volatile int* abort_flag) {
+                                                volatile sas::CtaCtl* abort_flag) {
   using IO = IoType<DT>;
   const int np = r1 - r0 + 1;  // <= kTmemMergeMax
   if (G.gst < 32) {
@@ -942,7 +944,7 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
 // never writes its partial.
 template <int DT>
 __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
-                                                 const Seg& sg, int r, int g, volatile int* abort_flag, bool tracing,
+                                                 const Seg& sg, int r, int g, volatile sas::CtaCtl* abort_flag, bool tracing,
                                                  unsigned long long* tr) {
   using IO = IoType<DT>;
   if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
@@ -1080,7 +1082,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
 // half's shared-memory writes before the second half's reads.
 template <int DT>
 __device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup& G, const SmShared& S, const Seg& sg,
-                                                    int g, volatile int* abort_flag) {
+                                                    int g, volatile sas::CtaCtl* abort_flag) {
   float l[32];
 #pragma unroll
   for (int h = 0; h < 32; ++h) l[h] = G.lsum[h];
@@ -1101,7 +1103,7 @@ __device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup&
 
 template <int DT>
 __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup& G, const SmShared& S,
-                                                     uint64_t* bars, const Seg& sg, int g, volatile int* abort_flag,
+                                                     uint64_t* bars, const Seg& sg, int g, volatile sas::CtaCtl* abort_flag,
                                                      bool tracing, unsigned long long* tr) {
   using IO = IoType<DT>;
   if (!twait(&bars[B_OFULL], G.seg & 1, abort_flag, p.status, 10, tracing, tr[TR_S_WAIT_O])) return false;
@@ -1146,7 +1148,7 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
 // so an uncovered cut token ends zero whatever the order of the pieces.
 template <int DT>
 __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us, const TokInfo* tok,
-                               const int* s_smax, const RangeInfo& ri, int g, volatile int* abort_flag) {
+                               const int* s_smax, const RangeInfo& ri, int g, volatile sas::CtaCtl* abort_flag) {
   using IO = IoType<DT>;
   sas::pdl_wait();  // the metadata is complete and visible
   const int smax = *s_smax;
@@ -1286,7 +1288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + (((raw_addr + 1023) & ~1023u) - raw_addr);
   uint8_t* misc = smem + OFF_MISC;
   uint64_t* bars = reinterpret_cast<uint64_t*>(misc + M_BAR);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + M_ABORT);
+  volatile sas::CtaCtl* abort_flag = reinterpret_cast<volatile sas::CtaCtl*>(misc + M_ABORT);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + M_TMEM);
   uint32_t* cmask = reinterpret_cast<uint32_t*>(misc + M_CMASK);        // [CD][4]
   int32_t* coords = reinterpret_cast<int32_t*>(misc + M_COORD);          // [CD][128]
@@ -1312,6 +1314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     sas::mbar_init(&bars[B_QFULL], 1);
     sas::mbar_init(&bars[B_QEMPTY], 1);
+    sas::mbar_init(&bars[B_DRAIN], 1);
     for (int i = 0; i < kTileChunks; ++i) sas::mbar_init(&bars[B_SF + i], 1);
     sas::mbar_init(&bars[B_OFULL], 1);
     sas::mbar_init(&bars[B_OEMPTY], 256);
@@ -1329,7 +1332,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<uint32_t*>(misc + M_SWORD)[i] = 0;
       reinterpret_cast<uint32_t*>(misc + M_LWORD)[i] = 0;
     }
-    *abort_flag = 0;
+    abort_flag->abort = 0;
+    abort_flag->limit_ns = p.wait_ns;
     sas::fence_mbar_init();
   }
   // heads beyond the Q box stay zero in every slab (H < 64)
@@ -1402,6 +1406,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool is_win = tl.c0 < p.n_win_chunks;  // a tile is all window or all compressed
       int coord[kTileChunks][4];
       bool val[kTileChunks][4];
+      // a block-table column past the table's width (a seqused_kv longer than
+      // the table) or an entry past the pool is dropped like a -1 entry, and
+      // reported (non-fatal) in the status word
+      bool bad = false;
       if (is_win) {
         const int lo = max(ti.s_g - p.win_left, 0);
 #pragma unroll
@@ -1410,8 +1418,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 4; ++k) {
             const int pos = lo + (tl.c0 + j) * CH + k * 32 + lane;
             val[j][k] = j < tl.nch && ti.s_g >= 0 && pos <= ti.s_g;
-            const int blk = val[j][k] ? p.ori_bt[(size_t)ti.b * p.ori_bt_stride + pos / p.ori_bs] : -1;
-            val[j][k] = val[j][k] && blk >= 0;
+            const int col = pos / p.ori_bs;
+            const bool in_table = col < p.ori_bt_stride;
+            const int blk = val[j][k] && in_table ? p.ori_bt[(size_t)ti.b * p.ori_bt_stride + col] : -1;
+            bad |= val[j][k] && (!in_table || blk >= p.ori_nblk);
+            val[j][k] = val[j][k] && blk >= 0 && blk < p.ori_nblk;
             coord[j][k] = blk * p.ori_bs + pos % p.ori_bs;
           }
       } else {
@@ -1450,11 +1461,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int id = coord[j][k];
-            const int blk = val[j][k] ? p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + id / p.cmp_bs] : -1;
-            val[j][k] = val[j][k] && blk >= 0;
+            const int col = id / p.cmp_bs;
+            const bool in_table = col < p.cmp_bt_stride;
+            const int blk = val[j][k] && in_table ? p.cmp_bt[(size_t)ti.b * p.cmp_bt_stride + col] : -1;
+            bad |= val[j][k] && (!in_table || blk >= p.cmp_nblk);
+            val[j][k] = val[j][k] && blk >= 0 && blk < p.cmp_nblk;
             coord[j][k] = val[j][k] ? blk * p.cmp_bs + id % p.cmp_bs : 0;
           }
       }
+      if (__any_sync(0xffffffffu, bad) && lane == 0 && p.status) atomicCAS(p.status, 0, SAS_ERR_BAD_BLOCK_ENTRY);
       if (tracing) tr[TR_P_COORD] += clock64() - tc0;
       if (TRACE && lane == 0 && tl.g0 == 0) ev(0);
       if (TRACE && lane == 0 && tl.g0 > 0 && tl.g0 <= (uint32_t)kTileChunks && !tl.first) ev(2);
@@ -1532,7 +1547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       return true;
     };
     Stream st;
-    uint32_t seg_i = 0;
+    uint32_t seg_i = 0, q_loads = 0;
     while (ok) {
       const int item = st.next<tracing>(bars, cinfo, abort_flag, p.status, tr[TR_P_WAIT_MASK]);
       if (item == SI_END) break;
@@ -1551,6 +1566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               sas::mbar_arrive_expect_tx(&bars[B_QFULL], q_bytes);
               for (int s = 0; s < NSLAB; ++s)
                 sas::tma_load_3d(smem + OFF_Q + s * Q_SLAB_BYTES, &tm_q, &bars[B_QFULL], s * 64, g * HG, ci.y);
+              ++q_loads;
             }
           }
           ++seg_i;
@@ -1566,6 +1582,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);
       }
     }
+    // nothing may still be landing in shared memory when the CTA exits (an
+    // aborted CTA leaves the loop with copies in flight)
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (tid == 0 && q_loads > 0) sas::mbar_wait_drain(&bars[B_QFULL], (q_loads - 1) & 1, SAS_WAIT_LIMIT_NS);
   } else if (warp == kMmaWarp) {
     // =============================== MMA issuer
     // Per tile: S^T of every chunk into its own TMEM slot as the K rows land,
@@ -1677,6 +1697,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (tracing) tr[TR_E_COPY] += clock64() - tv0;  // P.V section, waits included
         }
       }
+      // every MMA issued must be done before TMEM is freed (an aborted CTA
+      // leaves the loop with MMAs in flight)
+      sas::umma_commit(&bars[B_DRAIN]);
+      sas::mbar_wait_drain(&bars[B_DRAIN], 0, SAS_WAIT_LIMIT_NS);
     }
     __syncwarp();
   } else if (warp >= kSoftmaxWarp0) {
@@ -1835,6 +1859,9 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 float g_tau = 0.0f;  // exact running max (golden.py); > 0 only for experiments
 int g_cut_cost = -1; // tokens are never split across CTAs unless set
 unsigned long long* g_trace = nullptr;
+size_t g_trace_bytes = 0;  // size of the trace buffer
+int g_trace_dev = -1;      // the device that owns it
+unsigned long long g_wait_ns = SAS_WAIT_LIMIT_NS;
 
 struct WsLayout {
   size_t tok, unit, po, pl, cnt, total;
@@ -1863,7 +1890,32 @@ extern "C" int sas_fwd_set_option(int32_t option, double value, void* ptr) {
       g_tau = (float)value;
       return SAS_OK;
     case SAS_OPT_TRACE_BUFFER:
-      g_trace = static_cast<unsigned long long*>(ptr);
+      // value = the buffer's size in bytes; a launch on another device, or
+      // whose grid needs more than that, is refused
+      if (ptr == nullptr) {
+        g_trace = nullptr;
+        g_trace_bytes = 0;
+        g_trace_dev = -1;
+        return SAS_OK;
+      }
+      {
+        cudaPointerAttributes a;
+        if (!(value > 0.0) || cudaPointerGetAttributes(&a, ptr) != cudaSuccess || a.type != cudaMemoryTypeDevice) {
+          cudaGetLastError();
+          return SAS_ERR_INVALID_ARG;
+        }
+        g_trace = static_cast<unsigned long long*>(ptr);
+        g_trace_bytes = (size_t)value;
+        g_trace_dev = a.device;
+      }
+      return SAS_OK;
+    case SAS_OPT_WAIT_LIMIT_NS:
+      if (!(value >= 0.0 && value <= 60e9)) return SAS_ERR_INVALID_ARG;
+      g_wait_ns = value == 0.0 ? SAS_WAIT_LIMIT_NS : (unsigned long long)value;
+      return SAS_OK;
+    case SAS_OPT_SCHED_SCAN_CAP:
+      if (!(value >= 0.0 && value <= 4e18)) return SAS_ERR_INVALID_ARG;
+      sas::set_sched_scan_cap((long long)value);
       return SAS_OK;
     case SAS_OPT_SPLIT_TOKENS:
       if (!(value >= -1.0 && value <= 1e6)) return SAS_ERR_INVALID_ARG;
@@ -1953,8 +2005,6 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
                                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   alignas(64) CUtensorMap tm_q;
   const int q_box_h = std::min(HG, num_heads);
-  const int64_t ori_rows = ori_num_blocks * ori_block_size;
-  const int64_t cmp_rows = scenario >= 2 ? cmp_num_blocks * cmp_block_size : 0;
   if (!make_q_map(&tm_q, q, num_tokens, num_heads, q_box_h, tdt)) return SAS_ERR_CUDA;
 
   FwdParams fp{};
@@ -1971,8 +2021,8 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.ori_bt_stride = ori_table_stride;
   fp.cmp_bs = scenario >= 2 ? cmp_block_size : 1;
   fp.cmp_bt_stride = cmp_table_stride;
-  fp.ori_rows = (int)ori_rows;
-  fp.cmp_rows = (int)(scenario >= 2 ? cmp_rows : ori_rows);
+  fp.ori_nblk = (int)ori_num_blocks;
+  fp.cmp_nblk = (int)(scenario >= 2 ? cmp_num_blocks : ori_num_blocks);
   fp.ori_kv = static_cast<const uint8_t*>(ori_kv);
   fp.cmp_kv = static_cast<const uint8_t*>(scenario >= 2 ? cmp_kv : ori_kv);
   fp.ori_bt = ori_block_table;
@@ -1992,6 +2042,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.q_box_h = q_box_h;
   fp.tau = g_tau;
   fp.cut_cost = g_cut_cost;
+  fp.wait_ns = g_wait_ns;
   fp.fused = fused ? 1 : 0;
   fp.early = early ? 1 : 0;
   fp.B = batch;
@@ -2018,6 +2069,8 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
       return SAS_ERR_CUDA;
     attr_done |= 1ull << dev;
   }
+  if (fp.trace && (dev != g_trace_dev || g_trace_bytes < (size_t)R * G * (TR_NSLOTS + 16) * sizeof(uint64_t)))
+    return SAS_ERR_INVALID_ARG;
   if (stage_mask & SAS_STAGE_ATTENTION) {
     const bool tr = fp.trace != nullptr;
     const dim3 grid(R * G), block(kThreads);

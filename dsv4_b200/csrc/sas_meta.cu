@@ -37,6 +37,7 @@ struct MetaArgs {
   // derived (metadata.py:359-389)
   int64_t pre_token, next_token, group, m_base, s2_base;
   int is_s1g, is_cfa, is_scfa, att_mode;
+  int64_t scan_cap;  // rows the greedy walk may scan past a core's start before it reports an overrun
   int fast;  // row_info_fast applies (band mask, finite window, S1G layout)
   int smem;  // dynamic shared memory of this launch, bytes
 };
@@ -500,7 +501,7 @@ __device__ void assign_cores(const MetaArgs& A, const Arrays& V, int64_t B, int6
           bn2_cost = bn2_cost - all < 0 ? 0 : bn2_cost - all;
           base += 32;
           scanned += 32;
-          if (scanned > kRowScanCap) {
+          if (scanned > A.scan_cap) {
             overrun = true;
             break;
           }
@@ -688,7 +689,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+long long g_scan_cap = kRowScanCap;  // SAS_OPT_SCHED_SCAN_CAP
+
 }  // namespace
+
+namespace sas {
+void set_sched_scan_cap(long long cap) { g_scan_cap = cap > 0 ? cap : kRowScanCap; }
+}  // namespace sas
 
 extern "C" size_t sas_metadata_workspace_bytes(int32_t batch_size, int32_t aic_core_num) {
   const size_t b = batch_size > 0 ? (size_t)batch_size : 1;
@@ -740,6 +747,7 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
   A.win_left = ori_win_left;
   A.has_cmp = has_cmp_kv != 0;
   A.aic = aic_core_num;
+  A.scan_cap = g_scan_cap;
   // _params_init (metadata.py:359-389)
   if (ori_mask_mode == 0) {
     A.pre_token = kInt64Max;

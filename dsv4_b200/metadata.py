@@ -113,11 +113,14 @@ def sparse_attn_sharedkv_metadata(
 ) -> torch.Tensor:
     """Scheduler output ``int32[1024]`` (faMetadata[36][8] then fdMetadata[72][8]).
 
+    The schedule is always computed on a CUDA device. As in the reference
+    (metadata.py:1083-1086) the result is a CPU tensor unless ``device`` names
+    a CUDA device, in which case it stays there (no host synchronisation).
     ``out`` may supply a preallocated device ``int32[1024]`` buffer (e.g. for
-    CUDA-graph capture); it is returned.
+    CUDA-graph capture); it is filled and returned on its device.
     """
     del cu_seqlens_cmp_kv, ori_topk, cmp_mask_mode, ori_win_right, has_ori_kv, aiv_core_num
-    want_cpu = device is not None and torch.device(device).type == "cpu"
+    want_cpu = out is None and (device is None or torch.device(device).type == "cpu")
     if out is not None:
         dev = out.device
     elif device is not None and not want_cpu:

@@ -5,8 +5,9 @@
  * the current CUDA device; `stream` is a cudaStream_t passed as void*. The
  * library never allocates: every call that needs scratch takes a caller-owned
  * `workspace` whose size the matching *_workspace_bytes() function returns.
- * Calls are stateless and re-entrant; all work is enqueued on `stream` and
- * no call synchronises the host with the device.
+ * Calls keep no state between them (apart from the process-wide options of
+ * sas_fwd_set_option and the fixed scratch of sas_metadata_noalloc); all work
+ * is enqueued on `stream` and no call synchronises the host with the device.
  *
  * Return values are host-side argument/launch checks (SAS_OK or an SAS_ERR_*
  * code). Conditions only the device can see (a scheduler overrun, a bounded
@@ -30,6 +31,9 @@ extern "C" {
 #define SAS_ERR_WORKSPACE 4      /* workspace missing or smaller than required */
 #define SAS_ERR_SCHED_OVERRUN 5  /* device status: scheduler row scan hit its cap */
 #define SAS_ERR_NOALLOC_LIMIT 6  /* request exceeds the fixed scratch of sas_metadata_noalloc */
+#define SAS_ERR_BAD_BLOCK_ENTRY 7 /* device status, non-fatal: a block-table column past the table's width
+                                     (seqused_kv longer than the table) or an entry >= the pool's block
+                                     count was met; those rows were dropped like -1 entries */
 #define SAS_ERR_TIMEOUT_BASE 16  /* device status: 16 + id of the bounded wait that ran out */
 
 #define SAS_META_SIZE 1024
@@ -113,10 +117,14 @@ int sas_metadata_noalloc(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
  * Forward: the fused sparse shared-KV attention.
  * Replaces the device half of sparse_attn_sharedkv_tilelang/api.py:129-397
  * (the JIT kernel of kernel.py:56-1745 and its launch at api.py:372-384):
- * three launches on `stream` -- a plan kernel that walks the metadata's
- * per-core (bn2, m) windows (kernel.py:254-278) and sizes split-KV work for
- * every SM, the fused gather + tcgen05 attention kernel, and the split-KV
- * combine that folds the sink logit once.
+ * one or two launches on `stream`. Above 512 query tokens a single-CTA plan
+ * kernel first walks the metadata's per-core (bn2, m) windows
+ * (kernel.py:254-278) and lays out every token's softmax tiles; at or below
+ * 512 tokens every attention CTA builds that plan in its own shared memory and
+ * applies the metadata's coverage when it writes a token. The second launch
+ * is the fused gather + tcgen05 attention kernel. Tokens are never split
+ * across CTAs by default; with SAS_OPT_SPLIT_TOKENS the split-KV merge of a
+ * cut token runs inside the attention launch (no combine kernel).
  *
  *   q            [num_tokens, num_heads, 512] (TND) or [batch, S, num_heads, 512]
  *                (BSND, num_tokens = batch*S), bf16 or fp16, contiguous
@@ -162,7 +170,8 @@ int sas_sparse_attn_sharedkv_fwd(
  *     so P is rounded at the same points as golden.py. With value > 0 the max
  *     (and the accumulator) is only moved when a tile's max exceeds m by more
  *     than `value` (log2 units). Default 0: exact.
- *   SAS_OPT_TRACE_BUFFER (ptr): device buffer of 46 uint64 per CTA (30 per-role
+ *   SAS_OPT_TRACE_BUFFER (ptr, value = its size in bytes): device buffer of
+ *     46 uint64 per CTA (30 per-role
  *     cycle counters for every CTA, then 16 event timestamps per CTA) that
  *     receives the diagnostics of the next launches (NULL = off).
  *   SAS_OPT_SPLIT_TOKENS (value): by default a token is never split across
@@ -172,10 +181,24 @@ int sas_sparse_attn_sharedkv_fwd(
  *     few very long tokens, but a piece other than the first rounds P against
  *     its own running max, so such tokens meet the accuracy bounds and not the
  *     reference's rounding points. value < 0 restores the default.
+ *   SAS_OPT_WAIT_LIMIT_NS (value): limit, in ns, of every bounded wait of
+ *     the attention kernel for the next launches (0 restores the default of
+ *     2 s). A wait that runs out records SAS_ERR_TIMEOUT_BASE + its id in the
+ *     status word; the CTA drains the copies and MMAs it has in flight, frees
+ *     its TMEM and returns, so the context stays usable. Small values exist to
+ *     exercise that path.
+ *   SAS_OPT_SCHED_SCAN_CAP (value): rows the scheduler's greedy walk may scan
+ *     for one core before it stops and records SAS_ERR_SCHED_OVERRUN (0
+ *     restores the default of 2^24).
+ * These options are process-wide and not synchronised: set them while no
+ * other host thread is launching through this library. The trace buffer is
+ * one pointer for every device; it must hold 46 uint64 per CTA of the grid.
  * ---------------------------------------------------------------------- */
 #define SAS_OPT_RESCALE_THRESHOLD 1
 #define SAS_OPT_TRACE_BUFFER 2
 #define SAS_OPT_SPLIT_TOKENS 3
+#define SAS_OPT_WAIT_LIMIT_NS 4
+#define SAS_OPT_SCHED_SCAN_CAP 5
 int sas_fwd_set_option(int32_t option, double value, void* ptr);
 
 #ifdef __cplusplus

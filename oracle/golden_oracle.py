@@ -60,11 +60,40 @@ def round_dtype(x: np.ndarray, dtype: str) -> np.ndarray:
     raise ValueError(dtype)
 
 
+def paged_row_ids(table: np.ndarray, b: int, pos: np.ndarray, bs: int) -> np.ndarray:
+    """Flat pool row (block * bs + offset) of positions ``pos`` of request ``b``."""
+    pos = np.asarray(pos, np.int64)
+    return table[b, pos // bs].astype(np.int64) * bs + pos % bs
+
+
 def _paged_rows(pool: np.ndarray, table: np.ndarray, b: int, pos: np.ndarray) -> np.ndarray:
     """Rows ``pos`` of request ``b`` from a paged pool [nblk, bs, 1, D]."""
     bs = pool.shape[1]
     phys = table[b, pos // bs]
     return pool[phys, pos % bs, 0, :].astype(np.float32)
+
+
+def token_positions(*, s_g: int, idx_row: Optional[np.ndarray], has_cmp: bool, cmp_ratio: int, win_left: int):
+    """(window positions, compressed positions) one query token attends
+    (golden.py:28-66 and the window of golden.py:120-150)."""
+    win = np.arange(max(s_g - win_left, 0), s_g + 1) if s_g >= 0 else np.zeros(0, np.int64)
+    if not has_cmp:
+        return win, np.zeros(0, np.int64)
+    threshold = (s_g + 1) // cmp_ratio
+    if idx_row is not None:
+        return win, cmp_selected_positions(idx_row, threshold)
+    return win, np.arange(max(threshold, 0))
+
+
+def token_forward(q_t: np.ndarray, win: np.ndarray, cmp: np.ndarray, sinks: np.ndarray, softmax_scale: float,
+                  dtype: str = "bf16", s2_tile: int = GOLDEN_S2_TILE):
+    """One query token: ``q_t`` [H, D], attended rows ``win`` / ``cmp`` [n, D]
+    (float32 holding dtype values). Returns the dtype-rounded output [H, D]
+    and the LSE [H] (golden.py:156-204)."""
+    tiles = [win[i:i + s2_tile] for i in range(0, max(win.shape[0], 1), s2_tile)]
+    tiles += [cmp[i:i + s2_tile] for i in range(0, cmp.shape[0], s2_tile)]
+    o, l = _online_softmax(np.asarray(q_t, np.float32), tiles, np.asarray(sinks, np.float32), softmax_scale, dtype)
+    return round_dtype(o, dtype), l
 
 
 def cmp_selected_positions(idx_row: np.ndarray, threshold: int) -> np.ndarray:
@@ -175,12 +204,7 @@ def forward(
                 b=b, s_g=s_g, ori_kv=ori_kv, ori_bt=ori_bt, cmp_kv=cmp_kv, cmp_bt=cmp_bt,
                 idx_row=None if idx is None else idx[t, 0], cmp_ratio=cmp_ratio, win_left=win_left,
             )
-            tiles = [win[i:i + s2_tile] for i in range(0, max(win.shape[0], 1), s2_tile)]
-            tiles += [cmp[i:i + s2_tile] for i in range(0, cmp.shape[0], s2_tile)]
-            o, l = _online_softmax(q[t].astype(np.float32), tiles, np.asarray(sinks, np.float32),
-                                   softmax_scale, dtype)
-            out[t] = round_dtype(o, dtype)
-            lse[t] = l
+            out[t], lse[t] = token_forward(q[t], win, cmp, sinks, softmax_scale, dtype, s2_tile)
     return out, lse
 
 
@@ -221,6 +245,7 @@ def token_work(cu_seqlens_q, seqused_kv, idx, *, cmp_ratio=4, win_left=127, scen
 
 
 __all__ = [
-    "forward", "single_shot", "round_bf16", "round_dtype", "cmp_selected_positions",
+    "forward", "single_shot", "round_bf16", "round_dtype", "cmp_selected_positions", "paged_row_ids",
+    "token_positions", "token_forward",
     "token_rows", "token_work", "GOLDEN_S2_TILE",
 ]

@@ -140,3 +140,50 @@ def check_lse_ref(real, expt, dtype="bf16"):
     ok = np.isclose(real, expt, rtol=rtol, atol=atol, equal_nan=True)
     pct = ok.mean() * 100.0 if ok.size else 100.0
     assert pct >= 99.5, f"lse: only {pct:.4f}% within tolerance"
+
+
+def oracle_sampled(d, tokens, dtype="bf16", win_left=127):
+    """Oracle output and LSE for a sample of tokens of a device-resident case
+    ``d`` (the keyword dict of ``sparse_attn_sharedkv``, as built by
+    ``synth.make_case_torch``), at sizes whose full inputs the CPU could not
+    hold: only the sampled tokens' q rows and their attended KV rows are
+    gathered on the device and copied to the host; positions and the top-k
+    scan follow the oracle (``token_positions``), the math is ``token_forward``.
+    Returns ``(out [n, H, D], lse [n, H])`` in the order of ``tokens``."""
+    import torch
+    from oracle import golden_oracle as O
+
+    cu = d["cu_seqlens_q"].cpu().numpy().astype(np.int64)
+    skv = d["seqused_kv"].cpu().numpy().astype(np.int64)
+    ori_bt = d["ori_block_table"].cpu().numpy()
+    ori_bs = d["ori_kv"].shape[1]
+    ori_flat = d["ori_kv"].view(-1, d["ori_kv"].shape[-1])
+    has_cmp = "cmp_kv" in d
+    if has_cmp:
+        cmp_bt = d["cmp_block_table"].cpu().numpy()
+        cmp_bs = d["cmp_kv"].shape[1]
+        cmp_flat = d["cmp_kv"].view(-1, d["cmp_kv"].shape[-1])
+    idx = d.get("cmp_sparse_indices")
+    sinks = d["sinks"].float().cpu().numpy()
+    ratio = int(d.get("cmp_ratio", 4))
+    outs, lses = [], []
+    for t in tokens:
+        b = int(np.searchsorted(cu, t, side="right") - 1)
+        act_q = int(cu[b + 1] - cu[b])
+        s_g = int(skv[b]) - act_q + (t - int(cu[b]))
+        idx_row = idx[t, 0].cpu().numpy() if idx is not None else None
+        wpos, cpos = O.token_positions(s_g=s_g, idx_row=idx_row, has_cmp=has_cmp, cmp_ratio=ratio,
+                                       win_left=win_left)
+
+        def rows(flat, table, bs, pos):
+            if len(pos) == 0:
+                return np.zeros((0, flat.shape[1]), np.float32)
+            ids = torch.from_numpy(O.paged_row_ids(table, b, pos, bs)).to(flat.device)
+            return flat.index_select(0, ids).float().cpu().numpy()
+
+        win = rows(ori_flat, ori_bt, ori_bs, wpos)
+        cmp = rows(cmp_flat, cmp_bt, cmp_bs, cpos) if has_cmp else np.zeros((0, win.shape[1]), np.float32)
+        o, l = O.token_forward(d["q"][t].float().cpu().numpy(), win, cmp, sinks, float(d["softmax_scale"]), dtype)
+        outs.append(o)
+        lses.append(l)
+    return np.stack(outs), np.stack(lses)

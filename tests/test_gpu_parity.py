@@ -236,3 +236,15 @@ def test_deterministic_replay():
     a, la = U.run_api(case)
     b, lb = U.run_api(case)
     assert np.array_equal(a, b) and np.array_equal(la, lb)
+
+
+def test_metadata_default_returns_cpu_tensor():
+    """As the reference (metadata.py:1083-1086): a CPU tensor unless a device is named."""
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
+
+    kw = dict(num_heads_q=64, num_heads_kv=1, head_dim=512, cu_seqlens_q=torch.tensor([0, 1, 3], dtype=torch.int32),
+              seqused_kv=torch.tensor([5000, 900], dtype=torch.int32), batch_size=2, layout_q="TND", cmp_topk=512,
+              cmp_ratio=4)
+    a = sparse_attn_sharedkv_metadata(**kw)
+    b = sparse_attn_sharedkv_metadata(device="cuda", **kw)
+    assert a.device.type == "cpu" and b.is_cuda and torch.equal(a, b.cpu())

@@ -122,3 +122,23 @@ def test_metadata_drives_complete_coverage(name):
 def test_metadata_prefill_uses_many_cores():
     md = M.metadata(**_meta_kwargs(SCENARIOS["scfa_prefill"]))
     assert md[:288].reshape(36, 8)[:, 0].sum() == 24
+
+
+def test_sampled_oracle_matches_full_oracle():
+    """The sampled oracle used at full config shapes (rows gathered from
+    torch tensors) gives exactly what the full oracle gives on the same data."""
+    import torch
+    import sas_testutil as U
+    from dsv4_b200 import synth
+    from oracle import golden_oracle as O
+
+    d = synth.make_case_torch(ctx=[300, 2000, 130], q_lens=[2, 1, 3], H=16, K=256, bs=64, seed=5, device="cpu")
+    toks = [0, 1, 2, 4, 5]
+    so, sl = U.oracle_sampled(d, toks)
+    f32 = lambda t: t.float().numpy()
+    fo, fl = O.forward(f32(d["q"]), ori_kv=f32(d["ori_kv"]), ori_bt=d["ori_block_table"].numpy(),
+                       cmp_kv=f32(d["cmp_kv"]), cmp_bt=d["cmp_block_table"].numpy(),
+                       idx=d["cmp_sparse_indices"].numpy(), cu_seqlens_q=d["cu_seqlens_q"].numpy(),
+                       seqused_kv=d["seqused_kv"].numpy(), sinks=d["sinks"].numpy(),
+                       softmax_scale=d["softmax_scale"], cmp_ratio=4, tokens=toks)
+    assert np.array_equal(so, fo[toks]) and np.array_equal(sl, fl[toks])

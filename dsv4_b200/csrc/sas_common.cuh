@@ -71,13 +71,42 @@ struct CtaCtl {
   unsigned long long limit_ns;
 };
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Limits below this are met with non-blocking polls (mbarrier.test_wait,
+// the clock read after every poll): a blocking try_wait may sleep for longer
+// than such a limit before it reports that the phase is still open.
+constexpr uint64_t kPollLimitNs = 1000000ull;
+
 // Bounded wait. Returns false when the CTA is aborting or the limit ran out;
 // in the latter case status records SAS_ERR_TIMEOUT_BASE + where.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile CtaCtl* ctl, int* status,
                                           int where) {
+  const uint64_t lim = ctl->limit_ns;
+  if (lim < kPollLimitNs) {
+    const uint64_t t0 = globaltimer();
+    while (!mbar_test_wait(bar, parity)) {
+      if (ctl->abort) return false;
+      if (globaltimer() - t0 > lim) {
+        ctl->abort = 1;
+        if (status) atomicCAS(status, 0, SAS_ERR_TIMEOUT_BASE + where);
+        return false;
+      }
+    }
+    return true;
+  }
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  const uint64_t lim = ctl->limit_ns;
   uint32_t n = 0;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;

@@ -1,6 +1,6 @@
 """Benchmark of the sparse_attn_sharedkv forward on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C5] [--impl ours|reference]
 
 One step = one call of the op over one batch: the GPU scheduler
 (SparseAttnSharedkvMetadata) plus the fused attention (plan, attention,
@@ -11,11 +11,14 @@ runs its own batch (request-parallel, weak scaling: no collective on the data
 path) and the reported time is the max over ranks.
 
 Workloads (synthetic N(0,1) data, seeded):
-  C2 (default): bf16 decode, 64 requests x 1 token per GPU, 64 heads, K=512,
-      contexts U[8k, 64k], window 128, ratio 4, block 128.
-  C1, C3, C4: the CPU-golden decode, MTP decode and prefill configurations.
-  C5: long-context decode, 512 requests length-balanced over the N GPUs
-      (strong scaling), 128 heads, K=1024, contexts U[64k, 256k].
+  C5 (default): long-context decode, 512 requests length-balanced over the N
+      GPUs (strong scaling: the job is fixed, N=1 runs all 512), 128 heads,
+      K=1024, contexts U[64k, 256k], window 128, ratio 4, block 128. This is
+      the configuration BASELINE quotes at 1/2/4/8 GPUs.
+  C2: bf16 decode, 64 requests x 1 token per GPU (weak scaling), 64 heads,
+      K=512, contexts U[8k, 64k].
+  C1, C3, C4: the CPU-golden decode, MTP decode and prefill configurations
+      (per GPU, weak scaling).
 
 --mode heads (with any config): the head-sharded variant. Every rank holds
 every request and computes H/N heads; the outputs and LSEs are all-gathered
@@ -58,7 +61,7 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="C2", choices=["C1", "C2", "C3", "C4", "C5"])
+    ap.add_argument("--config", default="C5", choices=["C1", "C2", "C3", "C4", "C5"])
     ap.add_argument("--mode", default="requests", choices=["requests", "heads"],
                     help="requests: each rank runs its own requests (no collective); heads: every rank runs "
                          "H/N heads of all requests and the outputs are all-gathered over NCCL")
@@ -146,13 +149,55 @@ def algorithmic_work(d, H: int, K: int, ratio: int = 4, win_left: int = 127):
     return dict(bytes=byts, flops=flops, kv_rows=rows, tokens=T)
 
 
+# ------------------------------------------------------------------ profiles
+KERNEL_SOURCES = ("dsv4_b200/csrc/sas_fwd.cu", "dsv4_b200/csrc/sas_common.cuh")
+
+
+def kernel_source_sha256() -> str:
+    """Hash of the attention kernel's sources, stamped into every profile summary."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in KERNEL_SOURCES:
+        with open(os.path.join(ROOT, f), "rb") as fh:
+            h.update(fh.read())
+    return h.hexdigest()[:16]
+
+
+def profile_traffic(cfg: str, tokens: int):
+    """DRAM bytes per attention launch from the committed ncu summary of this
+    workload (profiles/sas_fwd_kernel_<config>_*.md: "traffic_bytes_per_launch",
+    "tokens_per_gpu", "kernel_source_sha256"). Only a summary taken on the
+    current kernel sources counts; otherwise traffic is null and the reason
+    is given."""
+    import glob
+
+    cur = kernel_source_sha256()
+    seen = []
+    for pf in sorted(glob.glob(os.path.join(ROOT, "profiles", f"sas_fwd_kernel_{cfg.lower()}_*.md"))):
+        kv = {}
+        for ln in open(pf):
+            if ":" in ln and ln.split(":")[0] in ("traffic_bytes_per_launch", "tokens_per_gpu", "kernel_source_sha256"):
+                k, v = ln.split(":", 1)
+                kv[k] = v.strip()
+        if "traffic_bytes_per_launch" not in kv or kv.get("tokens_per_gpu") != str(tokens):
+            continue
+        name = os.path.relpath(pf, ROOT)
+        if kv.get("kernel_source_sha256") == cur:
+            return int(kv["traffic_bytes_per_launch"]), {"profile": name, "kernel_source_sha256": cur}
+        seen.append(name)
+    why = ("profiles " + ", ".join(seen) + " were taken on other kernel sources") if seen else "no profile"
+    return None, {"profile": None, "kernel_source_sha256": cur, "note": why}
+
+
 # ------------------------------------------------------------------- clocks
 class ClockSampler:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{index}.csv") if os.path.isdir(
-            os.path.join(ROOT, "gpurun_out")) else f"/tmp/sas_clocks_gpu{index}.csv"
+        import tempfile
+
+        self.path = os.path.join(tempfile.gettempdir(), f"sas_clocks_{os.getpid()}_gpu{index}.csv")
 
     def __enter__(self):
         try:
@@ -308,6 +353,101 @@ def cpu_baseline(d, H, K, seconds: float):
     return {"value": done / dt, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
             "sample": f"{ntok} of {T} query tokens of the same workload, {done // ntok} passes ({dt:.1f} s); "
                       f"numpy restatement of golden.py (oracle/golden_oracle.py) with BLAS on all host threads"}
+
+
+# ------------------------------------------------------------------- e2e
+L2_BYTES = 126 * 1024 * 1024
+
+
+def e2e_pipelined(a, d, q, heads, world, dev, api, head_sharded, stream):
+    """Whole-job throughput through the public API with every step's inputs
+    copied up from pinned host memory and its results copied back, pipelined
+    over an input, a compute and an output stream with two device buffer sets.
+    When one step's KV rows would fit in L2, consecutive steps use different
+    top-k index sets (valid ids shifted by a per-set offset, modulo the valid
+    range) so that the rows a step reads were not left in L2 by the step
+    before. Returns (ms for a.steps steps, H2D bytes per step, D2H bytes per
+    step, description)."""
+    import torch
+
+    per_step_kv = 0
+    if "cmp_sparse_indices" in d:
+        per_step_kv = d["cmp_sparse_indices"].numel() * 1024
+    n_sets = 1 if per_step_kv == 0 else min(8, max(1, math.ceil(2 * L2_BYTES / max(per_step_kv, 1))))
+    keys = [k for k in ("cu_seqlens_q", "seqused_kv", "ori_block_table", "cmp_block_table", "cmp_sparse_indices",
+                        "sinks") if k in d]
+    host_sets = []
+    for j in range(n_sets):
+        hs = {k: d[k].cpu() for k in keys}
+        if j and "cmp_sparse_indices" in hs:
+            idx = hs["cmp_sparse_indices"].long()
+            cu = hs["cu_seqlens_q"].long()
+            skv = hs["seqused_kv"].long()
+            tok_b = torch.repeat_interleave(torch.arange(len(skv)), cu[1:] - cu[:-1])
+            s_pos = torch.arange(idx.shape[0]) - cu[tok_b]
+            thr = ((skv[tok_b] - (cu[1:] - cu[:-1])[tok_b] + s_pos + 1) // 4).clamp(min=1)[:, None, None]
+            shifted = torch.where(idx >= 0, (idx + 977 * j) % thr, idx)
+            hs["cmp_sparse_indices"] = shifted.to(torch.int32)
+        host_sets.append({k: v.contiguous().pin_memory() for k, v in hs.items()})
+    hq = q.cpu().pin_memory()
+    H = q.shape[1]
+    dev_sets = [dict({k: torch.empty_like(d[k]) for k in keys}, q=torch.empty_like(q)) for _ in range(2)]
+    outs = [(torch.empty_like(q), torch.empty((q.shape[0], H), dtype=torch.float32, device=dev)) for _ in range(2)]
+    houts = [(torch.empty(q.shape, dtype=q.dtype, pin_memory=True),
+              torch.empty((q.shape[0], H), dtype=torch.float32, pin_memory=True)) for _ in range(2)]
+    h2d = hq.numel() * hq.element_size() + sum(v.numel() * v.element_size() for v in host_sets[0].values())
+    d2h = houts[0][0].numel() * houts[0][0].element_size() + houts[0][1].numel() * 4
+    rest = {k: v for k, v in d.items() if k not in keys}
+    s_in, s_cmp, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    in_done = [torch.cuda.Event() for _ in range(2)]
+    cmp_done = [torch.cuda.Event() for _ in range(2)]
+    out_done = [torch.cuda.Event() for _ in range(2)]
+    started = [False, False]
+
+    def step(i):
+        b = i % 2
+        ds, hs = dev_sets[b], host_sets[i % n_sets]
+        with torch.cuda.stream(s_in):
+            if started[b]:
+                s_in.wait_event(cmp_done[b])  # the compute of step i-2 is done with this buffer set
+            ds["q"].copy_(hq, non_blocking=True)
+            for k in keys:
+                ds[k].copy_(hs[k], non_blocking=True)
+            in_done[b].record(s_in)
+        with torch.cuda.stream(s_cmp):
+            s_cmp.wait_event(in_done[b])
+            if started[b]:
+                s_cmp.wait_event(out_done[b])  # step i-2's results have left this output set
+            kw = dict(rest, **{k: ds[k] for k in keys})
+            o, l = outs[b]
+            if heads and world > 1:
+                oo, ll = head_sharded(ds["q"], **kw)
+                o.copy_(oo)
+                l.copy_(ll)
+            else:
+                api(ds["q"], out=o, lse_out=l, return_softmax_lse=True, **kw)
+            cmp_done[b].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(cmp_done[b])
+            houts[b][0].copy_(outs[b][0], non_blocking=True)
+            houts[b][1].copy_(outs[b][1], non_blocking=True)
+            out_done[b].record(s_out)
+        started[b] = True
+
+    for i in range(a.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for i in range(a.steps):
+        step(a.warmup + i)
+    s_out.wait_stream(s_in)
+    s_out.wait_stream(s_cmp)
+    e1.record(s_out)
+    torch.cuda.synchronize(dev)
+    note = (f"public API, pinned host buffers, H2D / compute / D2H pipelined over 3 streams; "
+            f"{n_sets} top-k index set(s) in rotation so consecutive steps read different KV rows")
+    return e0.elapsed_time(e1), h2d, d2h, note
 
 
 # ----------------------------------------------------------------- arms
@@ -467,41 +607,11 @@ def ours_arm(a, rank, world, local_rank):
 
     # e2e through the public API with pinned host inputs / outputs: every step
     # copies q and the per-step inputs host -> device and the results back
-    host = {}
-    for k in ("cu_seqlens_q", "seqused_kv", "ori_block_table", "cmp_block_table", "cmp_sparse_indices", "sinks"):
-        if k in d:
-            host[k] = d[k].cpu().pin_memory()
-    hq = q.cpu().pin_memory()
-    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    hlse = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
-    h2d = hq.numel() * hq.element_size() + sum(v.numel() * v.element_size() for v in host.values())
-    d2h = hout.numel() * hout.element_size() + hlse.numel() * hlse.element_size()
-    dd = {k: v for k, v in d.items()}
-
-    def e2e_step():
-        qd = hq.to(dev, non_blocking=True)
-        for k, v in host.items():
-            dd[k] = v.to(dev, non_blocking=True)
-        if heads and world > 1:
-            o, l = head_sharded_forward(qd, **dict(dd))
-        else:
-            o, l = sparse_attn_sharedkv(qd, return_softmax_lse=True, **dd)
-        hout.copy_(o, non_blocking=True)
-        hlse.copy_(l, non_blocking=True)
-
-    for _ in range(a.warmup):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    ev3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
-    for e0, e1 in ev3:
-        flush.zero_()
-        e0.record(stream)
-        e2e_step()
-        e1.record(stream)
-    torch.cuda.synchronize(dev)
-    e2e_ms = sum(e0.elapsed_time(e1) for e0, e1 in ev3)
-    if os.environ.get("SAS_BENCH_DEBUG"):
-        print("e2e per-step ms:", [round(e0.elapsed_time(e1), 3) for e0, e1 in ev3], file=sys.stderr)
+    # (D2H), pipelined over three streams as a serving loop would run it:
+    # step i+1's inputs go up while step i computes and step i-1's results come
+    # down (two device buffer sets). The window of K steps is timed whole.
+    e2e_ms, h2d, d2h, e2e_note = e2e_pipelined(a, d, q, heads, world, dev, sparse_attn_sharedkv,
+                                               head_sharded_forward, stream)
 
     # max over ranks
     t = torch.tensor([total_ms, e2e_ms, attn_ms], dtype=torch.float64, device=dev)
@@ -523,14 +633,7 @@ def ours_arm(a, rank, world, local_rank):
         peaks = json.load(open(pk))
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
     achieved = work["bytes"] / (attn_ms * 1e-3) / 1e9
-    # DRAM bytes per attention launch from the committed ncu capture of this
-    # workload (profiles/sas_fwd_kernel_<config>_*.md, "traffic_bytes_per_launch")
-    traffic = None
-    import glob
-    for pf in glob.glob(os.path.join(ROOT, "profiles", f"sas_fwd_kernel_{a.config.lower()}_*.md")):
-        for ln in open(pf):
-            if ln.startswith("traffic_bytes_per_launch:"):
-                traffic = int(ln.split(":")[1])
+    traffic, traffic_src = profile_traffic(a.config, T)
     value = tokens_all * a.steps / (total_ms * 1e-3)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
@@ -547,11 +650,11 @@ def ours_arm(a, rank, world, local_rank):
         "hbm_frac_of_8tbs": achieved / 8000.0,
         "tflops_attention": work["flops"] / (attn_ms * 1e-3) / 1e12,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "frac": achieved / hbm_peak, "traffic": traffic, "traffic_source": traffic_src,
                      "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if peaks else "fallback",
                      "algorithmic_bytes_per_launch": work["bytes"], "kernel": "sas_fwd_kernel"},
         "e2e": {"value": tokens_all * a.steps / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+                "d2h_bytes_per_step": d2h, "how": e2e_note},
         # our kernels per step: the scheduler and the attention kernel, plus
         # the plan kernel when the token count is above the fused-plan limit
         "gpu_launches": (2 if T <= FUSED_PLAN_MAX_TOKENS else 3) * a.steps,

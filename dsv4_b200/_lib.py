@@ -47,6 +47,8 @@ EXPORTS = {
     "sas_metadata_workspace_bytes": ([i32, i32], sz),
     "sas_metadata": ([vp, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
                       i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
+    "sas_metadata_fd": ([vp, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
+                         i32, i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
     "sas_fwd_workspace_bytes": ([i32, i32, i32], sz),
     "sas_fwd_set_option": ([i32, ctypes.c_double, vp], ctypes.c_int),
     "sas_sparse_attn_sharedkv_fwd": ([vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp, i32, vp, i64,

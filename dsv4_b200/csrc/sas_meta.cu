@@ -687,6 +687,384 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 
+// ---------------------------------------------------------------------------
+// Flash-decode (supportFd) variant of the scheduler: metadata.py with the
+// scheduler's supportFd flag set, which the reference declares and never
+// turns on (metadata.py:323-325). It differs from the default schedule in
+// four places: a core's cost limit is the plain average (not raised to the
+// largest row, 884-887), a core may end inside a row after the row walk
+// (AssignByBlock, 777-794; a core that took nothing is given one block,
+// 859-870, with the cursor rules of 829-857), a row cut between cores is
+// recorded as a flash-decode head (796-827), and the heads are spread over
+// the vector cores (925-954) into fdMetadata[72][8] (995-1009).
+// Phase 1 (per-batch costs) runs on the whole block, one thread per row;
+// the greedy walk is sequential by nature and runs on one thread.
+
+// Every field of _calc_s1g_cache (metadata.py:634-667) that the flash-decode
+// walk reads. With m_base == group the s1g tail is always zero, so only the
+// "normal" rows of the cost table apply.
+struct RowD {
+  int64_t cost, block, lbc, s2_start, s2_end, cmp_s2_start, win_nbc, win_lbc, cmp_nbc, cmp_lbc;
+};
+
+__device__ RowD row_detail(const MetaArgs& A, const BatchInfo& bi, int64_t idx) {
+  RowD r{};
+  if (bi.s1g_base == 0) return r;  // metadata.py:641-652: every field read here is zero
+  i128 first, last;
+  if (bi.s1 == 0 || bi.s2 == 0) {
+    first = 0;
+    last = 0;
+  } else if (!A.att_mode) {
+    first = 0;
+    last = bi.s2 - 1;
+  } else {
+    const int64_t g_first = idx * A.m_base;
+    const int64_t lim = bi.s1 * A.group;
+    const int64_t g_last = (g_first + A.m_base < lim ? g_first + A.m_base : lim) - 1;
+    int64_t f, l;
+    if (A.is_s1g) {
+      f = sas::floordiv64(g_first, A.group);
+      l = sas::floordiv64(g_last, A.group);
+    } else if (sas::floordiv64(g_first, bi.s1) == sas::floordiv64(g_last, bi.s1)) {
+      f = g_first - sas::floordiv64(g_first, bi.s1) * bi.s1;
+      l = g_last - sas::floordiv64(g_last, bi.s1) * bi.s1;
+    } else {
+      f = 0;
+      l = bi.s1;
+    }
+    first = (i128)f - bi.pre_lu;
+    last = (i128)l + bi.next_lu;
+  }
+  int64_t ol = 0, win_end = 0, win_tail = 0;
+  if (!(first >= bi.s2 || last < 0 || last < first)) {
+    const int64_t of = (int64_t)(first < 0 ? (i128)0 : (first > bi.s2 - 1 ? (i128)(bi.s2 - 1) : first));
+    ol = (int64_t)(last < 0 ? (i128)0 : (last > bi.s2 - 1 ? (i128)(bi.s2 - 1) : last));
+    win_end = sas::floordiv64(ol - of, A.s2_base) + 1;
+    const int64_t t = ol - of + 1;
+    win_tail = t - sas::floordiv64(t, A.s2_base) * A.s2_base;
+  }
+  const int64_t cmp_start = win_end;
+  const int64_t last_tok = (A.has_cmp && A.cmp_ratio > 0) ? sas::floordiv64(ol + 1, A.cmp_ratio) : 0;
+  int64_t act = 0;
+  if (A.is_cfa) act = last_tok;
+  else if (A.is_scfa) act = last_tok < A.cmp_topk ? last_tok : A.cmp_topk;
+  const int64_t cmp_end = act == 0 ? cmp_start : cmp_start + sas::floordiv64(act - 1, A.s2_base) + 1;
+  const int64_t cmp_tail = act - sas::floordiv64(act, A.s2_base) * A.s2_base;
+  const int64_t nn = calc_cost(A.m_base, A.s2_base);
+  int64_t win_block = 0, win_cost = 0;
+  if (0 < win_end) {
+    win_block = win_end;
+    const int64_t t = win_tail != 0 ? 1 : 0;
+    const int64_t w_nt = t ? calc_cost(A.m_base, win_tail) : 0;
+    win_cost = nn * (win_block - t) + w_nt * t;
+    r.win_lbc = t ? w_nt : nn;
+    r.win_nbc = nn;
+  }
+  int64_t cmp_block = 0, cmp_cost = 0;
+  if (cmp_start < cmp_end) {
+    cmp_block = cmp_end - cmp_start;
+    const int64_t t = cmp_tail != 0 ? 1 : 0;
+    const int64_t c_nt = t ? calc_cost(A.m_base, cmp_tail) : 0;
+    cmp_cost = nn * (cmp_block - t) + c_nt * t;
+    r.cmp_lbc = t ? c_nt : nn;
+    r.cmp_nbc = nn;
+  }
+  r.cmp_s2_start = cmp_start;
+  r.s2_start = win_block > 0 ? 0 : cmp_start;
+  if (cmp_block > 0) {
+    r.lbc = r.cmp_lbc;
+    r.s2_end = cmp_end;
+  } else {
+    r.lbc = r.win_lbc;
+    r.s2_end = win_end;
+  }
+  r.block = win_block + cmp_block;
+  r.cost = win_cost + cmp_cost;
+  return r;
+}
+
+constexpr int kFdHeads = SAS_AIC_CORE_NUM + 64;  // flash-decode heads (at most one per core boundary)
+constexpr int kFdVec = 72 + 64;                   // vector cores
+
+__global__ void __launch_bounds__(kThreads, 1)
+    sas_metadata_fd_kernel(MetaArgs A, int64_t aiv, long long* __restrict__ ws, int64_t* __restrict__ core_out,
+                           int32_t* __restrict__ meta_out, int32_t* status) {
+  sas::pdl_launch_dependents();
+  __shared__ int s_all_zero;
+  __shared__ long long s_max_cost, s_total;
+  __shared__ int64_t s_used, s_nvec;
+  __shared__ int64_t f_bn2[kFdHeads], f_m[kFdHeads], f_ws[kFdHeads], f_split[kFdHeads], f_msz[kFdHeads];
+  __shared__ int64_t v_idx[kFdVec], v_mstart[kFdVec], v_mnum[kFdVec];
+  const int tid = threadIdx.x;
+  const int64_t B = A.batch;
+  const int64_t B1 = B > 0 ? B : 1;
+  long long* cost = ws;           // per batch: cost, blocks, last row with blocks, row prefix
+  long long* blocks = cost + B1;
+  long long* last_row = blocks + B1;
+  long long* rows = last_row + B1;  // B + 1: rows before batch b
+  if (tid == 0) {
+    s_all_zero = 1;
+    s_max_cost = 0;
+    s_total = 0;
+    s_used = 1;
+    s_nvec = 0;
+  }
+  __syncthreads();
+  // split info (metadata.py:671-683); a batch's rows are costed only when
+  // both of its lengths are non-zero (metadata.py:687-689)
+  for (int64_t b = tid; b < B; b += kThreads) {
+    const int64_t s1 = s1_size(A, b), s2 = s2_size(A, b);
+    const BatchInfo bi = make_bi(A, s1, s2);
+    const int64_t s2b = sas::floordiv64(s2 + A.s2_base - 1, A.s2_base);
+    if (bi.s1g_base != 0 && s2b != 0) s_all_zero = 0;
+    cost[b] = 0;
+    blocks[b] = 0;
+    last_row[b] = -1;
+    rows[b] = (s1 == 0 || s2 == 0) ? 0 : bi.s1g_base;
+  }
+  __syncthreads();
+  if (tid == 0) {  // exclusive prefix of the costed rows (small batches: one pass)
+    long long run = 0;
+    for (int64_t b = 0; b < B; ++b) {
+      const long long n = rows[b];
+      rows[b] = run;
+      run += n;
+    }
+    rows[B] = run;
+  }
+  __syncthreads();
+  if (!s_all_zero) {
+    // per-row costs (metadata.py:685-714), one thread per row
+    const long long nrows = rows[B];
+    for (long long r = tid; r < nrows; r += kThreads) {
+      int64_t lo = 0, hi = B - 1;  // last batch with rows[b] <= r
+      while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (rows[mid] <= r) lo = mid;
+        else hi = mid - 1;
+      }
+      const int64_t b = lo, row = r - rows[b];
+      const BatchInfo bi = make_bi(A, s1_size(A, b), s2_size(A, b));
+      const RowD d = row_detail(A, bi, row);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&cost[b]), (unsigned long long)d.cost);
+      atomicAdd(reinterpret_cast<unsigned long long*>(&blocks[b]), (unsigned long long)d.block);
+      atomicMax(&s_max_cost, (long long)d.cost);
+      if (d.block > 0) atomicMax(&last_row[b], (long long)row);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      // the greedy walk (metadata.py:872-923) with the flash-decode steps
+      for (int64_t b = 0; b < B; ++b) s_total += cost[b] * A.nkv;
+      auto lbc_of = [&](int64_t b) -> int64_t {  // bn2_last_block_cost_of_each_batch
+        if (last_row[b] < 0) return 0;
+        return row_detail(A, make_bi(A, s1_size(A, b), s2_size(A, b)), last_row[b]).lbc;
+      };
+      int64_t cur_b = 0, cur_bn2 = 0, cur_s1g = 0, cur_s2 = 0, cur_core = 0;
+      int64_t unassigned = s_total, bn2_cost = cost[0], bn2_block = blocks[0];
+      int64_t split_part = 1;
+      const int64_t fd_data_num = 1;  // never advanced in metadata.py
+      int64_t n_head = 0;
+      bool finished = false, overrun = false;
+      BatchInfo bi = make_bi(A, s1_size(A, 0), s2_size(A, 0));
+      RowD sc = row_detail(A, bi, 0);
+      cur_s2 = sc.s2_start;
+      auto new_row = [&](int64_t idx) {
+        cur_s1g = idx;
+        sc = row_detail(A, bi, idx);
+      };
+      auto block_cost = [&]() -> int64_t {  // metadata.py:766-775
+        if (cur_s2 < sc.cmp_s2_start) return cur_s2 == sc.cmp_s2_start - 1 ? sc.win_lbc : sc.win_nbc;
+        return cur_s2 == sc.s2_end - 1 ? sc.cmp_lbc : sc.cmp_nbc;
+      };
+      for (int64_t i = 0; i < A.aic; ++i) {
+        if (finished || unassigned <= 0) break;
+        cur_core = i;
+        const int64_t den = A.aic - cur_core > 1 ? A.aic - cur_core : 1;
+        const int64_t limit = sas::floordiv64(unassigned, den);
+        int64_t ccost = 0, cblock = 0;
+        // AssignByBatch (718-745)
+        while (!finished && (bn2_cost == 0 || limit + sas::floordiv64(lbc_of(cur_b), 2) >= ccost + bn2_cost)) {
+          ccost += bn2_cost;
+          cblock += bn2_block;
+          cur_bn2 += 1;
+          if (cur_bn2 == B * A.nkv) {
+            cur_s1g = 0;
+            cur_s2 = 0;
+            finished = true;
+            break;
+          }
+          if (sas::floordiv64(cur_bn2, A.nkv) != cur_b) {
+            cur_b = sas::floordiv64(cur_bn2, A.nkv);
+            bi = make_bi(A, s1_size(A, cur_b), s2_size(A, cur_b));
+          }
+          bn2_cost = cost[cur_b];
+          bn2_block = blocks[cur_b];
+          new_row(0);
+          cur_s2 = sc.s2_start;
+        }
+        // AssignByRow (747-764)
+        if (!finished) {
+          int64_t scanned = 0;
+          while (limit + sas::floordiv64(sc.lbc, 2) >= ccost + sc.cost) {
+            ccost += sc.cost;
+            cblock += sc.block;
+            bn2_cost = bn2_cost - sc.cost < 0 ? 0 : bn2_cost - sc.cost;
+            bn2_block = bn2_block - sc.block < 0 ? 0 : bn2_block - sc.block;
+            do {
+              new_row(cur_s1g + 1);
+              if (++scanned > A.scan_cap) overrun = true;
+            } while (sc.block == 0 && !overrun);
+            cur_s2 = sc.s2_start;
+            if (overrun) break;
+          }
+        }
+        if (overrun) break;
+        // AssignByBlock (777-794)
+        if (!finished) {
+          int64_t c = block_cost();
+          int64_t scanned = 0;
+          while (limit + sas::floordiv64(c, 2) >= ccost + c) {
+            ccost += c;
+            cblock += 1;
+            cur_s2 += 1;
+            bn2_cost -= c;
+            sc.cost -= c;
+            bn2_block -= 1;
+            sc.block -= 1;
+            c = block_cost();
+            if (++scanned > A.scan_cap) {
+              overrun = true;
+              break;
+            }
+          }
+        }
+        if (overrun) break;
+        // ForceAssign (859-870) with UpdateCursor (829-857)
+        if (cblock == 0 && !finished) {
+          const int64_t c = block_cost();
+          ccost += c;
+          cblock += 1;
+          cur_s2 += 1;
+          bn2_cost -= c;
+          bn2_block -= 1;
+          sc.cost -= c;
+          sc.block -= 1;
+          bool upd_row = false, upd_b = false;
+          if (cur_s2 >= sc.s2_end) {
+            cur_s2 = 0;
+            cur_s1g += 1;
+            upd_row = true;
+          }
+          if (cur_s1g >= bi.s1g_base) {
+            cur_s1g = 0;
+            cur_bn2 += 1;
+          }
+          if (cur_bn2 == B * A.nkv) {
+            cur_s1g = 0;
+            cur_s2 = 0;
+            finished = true;
+          } else {
+            if (sas::floordiv64(cur_bn2, A.nkv) != cur_b) {
+              cur_b = sas::floordiv64(cur_bn2, A.nkv);
+              cur_s1g = 0;
+              upd_b = true;
+              upd_row = true;
+            }
+            if (upd_b) {
+              bi = make_bi(A, s1_size(A, cur_b), s2_size(A, cur_b));
+              bn2_cost = cost[cur_b];
+              bn2_block = blocks[cur_b];
+            }
+            if (upd_row) {
+              new_row(cur_s1g);
+              cur_s2 = 0;  // win_s2_start, always 0
+            }
+          }
+        }
+        core_out[3 * i + 0] = cur_bn2;
+        core_out[3 * i + 1] = cur_s1g;
+        core_out[3 * i + 2] = cur_s2;
+        unassigned -= ccost;
+        // a row cut between this core and the one before (796-827)
+        if (cur_core != 0 && split_part > 1 &&
+            !(cur_bn2 == core_out[3 * (i - 1)] && cur_s1g == core_out[3 * (i - 1) + 1])) {
+          if (n_head >= A.aic || n_head >= kFdHeads) {
+            overrun = true;
+            break;
+          }
+          const int64_t sb = sas::floordiv64(core_out[3 * (i - 1)], A.nkv);
+          const int64_t srow = core_out[3 * (i - 1) + 1];
+          const BatchInfo sbi = make_bi(A, s1_size(A, sb), s2_size(A, sb));
+          f_bn2[n_head] = core_out[3 * (i - 1)];
+          f_m[n_head] = srow;
+          f_ws[n_head] = fd_data_num - split_part;
+          f_split[n_head] = split_part;
+          f_msz[n_head] = srow == sbi.s1g_base - 1 ? sbi.s1 * A.group - srow * A.m_base : A.m_base;
+          n_head += 1;
+          split_part = 1;
+        }
+        if (sc.s2_start < cur_s2 && cur_s2 <= sc.s2_end) split_part += 1;
+      }
+      if (overrun && status) atomicCAS(status, 0, SAS_ERR_SCHED_OVERRUN);
+      s_used = cur_core + 1;
+      // the heads over the vector cores (925-954)
+      long long total_fd = 0;
+      for (int64_t h = 0; h < n_head; ++h) total_fd += f_split[h] * f_msz[h];
+      const int64_t avg = aiv > 0 ? sas::floordiv64(total_fd, aiv) : 0;
+      int64_t cur = 0;
+      if (n_head > 0 && avg > 0) {
+        for (int64_t h = 0; h < n_head; ++h) {
+          const int64_t nv = sas::floordiv64(f_split[h] * f_msz[h], avg);
+          if (nv == 0) continue;
+          const int64_t ave = sas::floordiv64(f_msz[h], nv);
+          for (int64_t v = 0; v < nv; ++v) {
+            if (cur >= aiv || cur >= kFdVec) break;
+            v_idx[cur] = h;
+            v_mstart[cur] = v * ave;
+            v_mnum[cur] = v < nv - 1 ? ave : f_msz[h] - v * ave;
+            ++cur;
+          }
+        }
+      }
+      s_nvec = cur;
+    }
+  } else if (tid == 0) {  // metadata.py:959-964
+    core_out[0] = B * A.nkv;
+    core_out[1] = 0;
+    core_out[2] = 0;
+  }
+  __syncthreads();
+  // pack (metadata.py:974-1009)
+  const int64_t used = s_used, nvec = s_nvec;
+  for (int i = tid; i < SAS_META_SIZE; i += kThreads) {
+    int32_t v = 0;
+    if (i < SAS_AIC_CORE_NUM * 8) {
+      const int core = i >> 3, f = i & 7;
+      if (core < used && core < A.aic) {
+        if (f == 0) v = 1;
+        else if (f <= 3) v = core == 0 ? 0 : (int32_t)core_out[3 * (core - 1) + (f - 1)];
+        else if (f <= 6) v = (int32_t)core_out[3 * core + (f - 4)];
+      }
+    } else {
+      const int j = i - SAS_AIC_CORE_NUM * 8, vc = j >> 3, f = j & 7;
+      if (vc < nvec && vc < aiv) {
+        const int64_t h = v_idx[vc];
+        switch (f) {
+          case 0: v = 1; break;
+          case 1: v = (int32_t)f_bn2[h]; break;
+          case 2: v = (int32_t)f_m[h]; break;
+          case 3: v = (int32_t)f_ws[h]; break;
+          case 4: v = (int32_t)f_split[h]; break;
+          case 5: v = (int32_t)v_mstart[vc]; break;
+          case 6: v = (int32_t)v_mnum[vc]; break;
+          default: v = 0;
+        }
+      }
+    }
+    meta_out[i] = v;
+  }
+}
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 long long g_scan_cap = kRowScanCap;  // SAS_OPT_SCHED_SCAN_CAP
@@ -703,14 +1081,15 @@ extern "C" size_t sas_metadata_workspace_bytes(int32_t batch_size, int32_t aic_c
   return align_up(sizeof(long long) * (kNumArrays * b + 1), 256) + align_up(sizeof(int64_t) * 3 * c, 256);
 }
 
-extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q, const int32_t* cu_seqlens_ori_kv,
+namespace {
+int metadata_launch(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q, const int32_t* cu_seqlens_ori_kv,
                             int32_t n_cu_seqlens_ori_kv, const int32_t* seqused_q, int32_t n_seqused_q,
                             const int32_t* seqused_kv, int32_t n_seqused_kv, int32_t batch_size,
                             int32_t max_seqlen_q, int32_t max_seqlen_kv, int32_t num_heads_q,
                             int32_t num_heads_kv, int32_t head_dim, int32_t cmp_topk, int32_t cmp_ratio,
                             int32_t ori_mask_mode, int32_t ori_win_left, int32_t layout_q, int32_t layout_kv,
                             int32_t has_cmp_kv, int32_t aic_core_num, int32_t* metadata_out, int32_t* status,
-                            void* workspace, size_t workspace_bytes, void* stream) {
+                            void* workspace, size_t workspace_bytes, void* stream, bool support_fd, int32_t aiv_core_num) {
   (void)head_dim;
   if (!metadata_out) return SAS_ERR_INVALID_ARG;
   if (!sas::select_device_of(metadata_out)) return SAS_ERR_INVALID_ARG;
@@ -800,9 +1179,45 @@ extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
       attr_done |= 1ull << (dev & 63);
     }
   }
-  sas_metadata_kernel<<<1, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(A, arrays, core_out, metadata_out,
-                                                                                status);
+  if (support_fd) {
+    sas_metadata_fd_kernel<<<1, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(A, aiv_core_num, arrays, core_out,
+                                                                                 metadata_out, status);
+  } else {
+    sas_metadata_kernel<<<1, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(A, arrays, core_out,
+                                                                                  metadata_out, status);
+  }
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+}
+}  // namespace
+
+extern "C" int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q, const int32_t* cu_seqlens_ori_kv,
+                            int32_t n_cu_seqlens_ori_kv, const int32_t* seqused_q, int32_t n_seqused_q,
+                            const int32_t* seqused_kv, int32_t n_seqused_kv, int32_t batch_size,
+                            int32_t max_seqlen_q, int32_t max_seqlen_kv, int32_t num_heads_q,
+                            int32_t num_heads_kv, int32_t head_dim, int32_t cmp_topk, int32_t cmp_ratio,
+                            int32_t ori_mask_mode, int32_t ori_win_left, int32_t layout_q, int32_t layout_kv,
+                            int32_t has_cmp_kv, int32_t aic_core_num, int32_t* metadata_out, int32_t* status,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  return metadata_launch(cu_seqlens_q, n_cu_seqlens_q, cu_seqlens_ori_kv, n_cu_seqlens_ori_kv, seqused_q, n_seqused_q,
+                         seqused_kv, n_seqused_kv, batch_size, max_seqlen_q, max_seqlen_kv, num_heads_q, num_heads_kv,
+                         head_dim, cmp_topk, cmp_ratio, ori_mask_mode, ori_win_left, layout_q, layout_kv, has_cmp_kv,
+                         aic_core_num, metadata_out, status, workspace, workspace_bytes, stream, false, 0);
+}
+
+extern "C" int sas_metadata_fd(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
+                               const int32_t* cu_seqlens_ori_kv, int32_t n_cu_seqlens_ori_kv,
+                               const int32_t* seqused_q, int32_t n_seqused_q, const int32_t* seqused_kv,
+                               int32_t n_seqused_kv, int32_t batch_size, int32_t max_seqlen_q, int32_t max_seqlen_kv,
+                               int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim, int32_t cmp_topk,
+                               int32_t cmp_ratio, int32_t ori_mask_mode, int32_t ori_win_left, int32_t layout_q,
+                               int32_t layout_kv, int32_t has_cmp_kv, int32_t aic_core_num, int32_t aiv_core_num,
+                               int32_t* metadata_out, int32_t* status, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  if (aiv_core_num < 0 || aiv_core_num > 72 + 64 || aic_core_num > SAS_AIC_CORE_NUM + 64) return SAS_ERR_INVALID_ARG;
+  return metadata_launch(cu_seqlens_q, n_cu_seqlens_q, cu_seqlens_ori_kv, n_cu_seqlens_ori_kv, seqused_q, n_seqused_q,
+                         seqused_kv, n_seqused_kv, batch_size, max_seqlen_q, max_seqlen_kv, num_heads_q, num_heads_kv,
+                         head_dim, cmp_topk, cmp_ratio, ori_mask_mode, ori_win_left, layout_q, layout_kv, has_cmp_kv,
+                         aic_core_num, metadata_out, status, workspace, workspace_bytes, stream, true, aiv_core_num);
 }
 
 // ---------------------------------------------------------------------------

@@ -110,6 +110,7 @@ def sparse_attn_sharedkv_metadata(
     aiv_core_num: int = 48,
     device: Optional[str] = None,
     out: Optional[torch.Tensor] = None,
+    support_fd: bool = False,
 ) -> torch.Tensor:
     """Scheduler output ``int32[1024]`` (faMetadata[36][8] then fdMetadata[72][8]).
 
@@ -118,8 +119,12 @@ def sparse_attn_sharedkv_metadata(
     a CUDA device, in which case it stays there (no host synchronisation).
     ``out`` may supply a preallocated device ``int32[1024]`` buffer (e.g. for
     CUDA-graph capture); it is filled and returned on its device.
+    ``support_fd=True`` computes the flash-decode schedule: the reference
+    scheduler with its ``supportFd`` switch on (metadata.py:323-325, left
+    False by the reference), whose cores may end inside a row and whose
+    ``fdMetadata`` rows spread the cut rows over ``aiv_core_num`` vector cores.
     """
-    del cu_seqlens_cmp_kv, ori_topk, cmp_mask_mode, ori_win_right, has_ori_kv, aiv_core_num
+    del cu_seqlens_cmp_kv, ori_topk, cmp_mask_mode, ori_win_right, has_ori_kv
     want_cpu = out is None and (device is None or torch.device(device).type == "cpu")
     if out is not None:
         dev = out.device
@@ -159,11 +164,15 @@ def sparse_attn_sharedkv_metadata(
     def n(t):
         return 0 if t is None else t.numel()
 
-    rc = lib.sas_metadata(
-        _lib.ptr(cu_q), n(cu_q), _lib.ptr(cu_kv), n(cu_kv), _lib.ptr(sq), n(sq), _lib.ptr(skv), n(skv),
-        int(batch_size), int(max_seqlen_q), int(max_seqlen_kv), int(num_heads_q), int(num_heads_kv), int(head_dim),
-        int(cmp_topk), int(cmp_ratio), int(ori_mask_mode), int(ori_win_left), lq, lkv, int(bool(has_cmp_kv)),
-        int(aic_core_num), out.data_ptr(), st.status.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    args = (_lib.ptr(cu_q), n(cu_q), _lib.ptr(cu_kv), n(cu_kv), _lib.ptr(sq), n(sq), _lib.ptr(skv), n(skv),
+            int(batch_size), int(max_seqlen_q), int(max_seqlen_kv), int(num_heads_q), int(num_heads_kv),
+            int(head_dim), int(cmp_topk), int(cmp_ratio), int(ori_mask_mode), int(ori_win_left), lq, lkv,
+            int(bool(has_cmp_kv)), int(aic_core_num))
+    tail = (out.data_ptr(), st.status.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    if support_fd:
+        rc = lib.sas_metadata_fd(*args, int(aiv_core_num), *tail)
+    else:
+        rc = lib.sas_metadata(*args, *tail)
     if rc == 1:
         raise ValueError("sparse_attn_sharedkv_metadata: invalid arguments (array lengths / heads / ratio)")
     _lib.check(rc, "sas_metadata")

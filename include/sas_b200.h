@@ -90,6 +90,27 @@ int sas_metadata(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
                  int32_t* metadata_out, int32_t* status,
                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* Flash-decode schedule: the same scheduler with the reference's supportFd
+ * switch on (sparse_attn_sharedkv_tilelang/metadata.py:323-325, which the
+ * reference declares and leaves False). Replaces the supportFd branches of
+ * metadata.py:777-870 (a core may end inside a row, AssignByBlock /
+ * ForceAssign; rows cut between cores become flash-decode heads) and
+ * 925-954 (the heads spread over aiv_core_num vector cores). fdMetadata[72][8]
+ * = (enable, bn2_idx, m_idx, workspace_idx, workspace_num, m_start, m_num, 0)
+ * per vector core. Same arguments, workspace and bit-exact contract as
+ * sas_metadata plus aiv_core_num (metadata.py:1043, default 48); the forward
+ * kernel accepts either schedule (it reads the per-core (bn2, m) windows). */
+int sas_metadata_fd(const int32_t* cu_seqlens_q, int32_t n_cu_seqlens_q,
+                    const int32_t* cu_seqlens_ori_kv, int32_t n_cu_seqlens_ori_kv,
+                    const int32_t* seqused_q, int32_t n_seqused_q,
+                    const int32_t* seqused_kv, int32_t n_seqused_kv,
+                    int32_t batch_size, int32_t max_seqlen_q, int32_t max_seqlen_kv,
+                    int32_t num_heads_q, int32_t num_heads_kv, int32_t head_dim,
+                    int32_t cmp_topk, int32_t cmp_ratio, int32_t ori_mask_mode, int32_t ori_win_left,
+                    int32_t layout_q, int32_t layout_kv, int32_t has_cmp_kv, int32_t aic_core_num,
+                    int32_t aiv_core_num, int32_t* metadata_out, int32_t* status,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of sas_metadata. No counterpart in the reference.
  * For callers that cannot allocate device memory when they need a schedule
  * (code running inside an allocator or teardown path, plugins whose host owns

@@ -39,7 +39,7 @@ def _load():
         _lib = ctypes.CDLL(build())
         P = ctypes.POINTER(ctypes.c_int64)
         I = ctypes.c_int64
-        _lib.sas_meta_oracle.argtypes = [I, I, I, P, I, P, I, P, I, P, I, I, I, I, I, I, I, I, I, I, I, I,
+        _lib.sas_meta_oracle.argtypes = [I, I, I, P, I, P, I, P, I, P, I, I, I, I, I, I, I, I, I, I, I, I, I, I,
                                          ctypes.POINTER(ctypes.c_int32)]
         _lib.sas_meta_oracle.restype = ctypes.c_int
     return _lib
@@ -58,7 +58,9 @@ def metadata(*, num_heads_q, num_heads_kv, head_dim, cu_seqlens_q=None, cu_seqle
              cu_seqlens_cmp_kv=None, seqused_q=None, seqused_kv=None, batch_size=0, max_seqlen_q=0,
              max_seqlen_kv=0, ori_topk=0, cmp_topk=0, cmp_ratio=-1, ori_mask_mode=4, cmp_mask_mode=3,
              ori_win_left=127, ori_win_right=0, layout_q="BSND", layout_kv="PA_ND", has_ori_kv=True,
-             has_cmp_kv=True, aic_core_num=24, aiv_core_num=48) -> np.ndarray:
+             has_cmp_kv=True, aic_core_num=24, aiv_core_num=48, support_fd=False) -> np.ndarray:
+    """The scheduler's int32[1024] output; ``support_fd`` runs the reference
+    scheduler's flash-decode branches (its ``supportFd`` switch)."""
     lib = _load()
     keep = []
 
@@ -78,7 +80,8 @@ def metadata(*, num_heads_q, num_heads_kv, head_dim, cu_seqlens_q=None, cu_seqle
         int(num_heads_q), int(num_heads_kv), int(head_dim), cq, ncq, ck, nck, sq, nsq, sk, nsk,
         int(batch_size), int(max_seqlen_q), int(max_seqlen_kv), int(cmp_topk), int(cmp_ratio),
         int(ori_mask_mode), int(ori_win_left), LAYOUT_Q.get(layout_q, 3), LAYOUT_KV.get(layout_kv, 0),
-        int(bool(has_cmp_kv)), int(aic_core_num), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
+        int(bool(has_cmp_kv)), int(aic_core_num), int(aiv_core_num), int(bool(support_fd)),
+        out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)))
     if rc != 0:
         raise RuntimeError(f"metadata oracle failed with status {rc}")
     return out

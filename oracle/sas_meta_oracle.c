@@ -12,8 +12,12 @@
  *   cost table            metadata.py:428-477
  *   win / cmp s1g caches  metadata.py:549-621, gather 623-632, s1g 634-667
  *   split info / costs    metadata.py:671-714
- *   assign by batch/row   metadata.py:718-764 (supportFd=False, so the
- *                         block/FD paths 766-954 are never reached)
+ *   assign by batch/row   metadata.py:718-764
+ *   flash-decode path     metadata.py:766-870, 925-954 (only with support_fd,
+ *                         which the reference's scheduler leaves False,
+ *                         metadata.py:323-325): assign by block 777-794,
+ *                         FD records 796-827, cursor / force assign 829-870,
+ *                         FD vector split 925-954
  *   per-core plan         metadata.py:872-923, schedule 956-972
  *   packing               metadata.py:974-1009
  * Python integers are unbounded; the few quantities that can exceed int64
@@ -58,7 +62,7 @@ typedef struct {
   int64_t layout_q; /* 0 BSND, 1 TND, 2 BSH, 3 other */
   int64_t layout_kv; /* 0 PA_ND, 1 TND */
   int64_t has_cmp;
-  int64_t aic;
+  int64_t aic, aiv, support_fd;
   /* derived */
   int64_t pre_token, next_token, group, m_base, s2_base;
   int is_s1g, is_cfa, is_scfa, attention_mode;
@@ -231,6 +235,7 @@ static void s1g_cache(Sched *S, int64_t s1g, Ctx *C, BatchC *bc, S1GC *sc) {
 
 typedef struct {
   int64_t cur_b, cur_bn2, cur_s1g, cur_s2, cur_core, unassigned, bn2_cost, bn2_block;
+  int64_t kv_split_part, fd_data_num;
   int finished;
   BatchC bc;
   S1GC sc;
@@ -273,6 +278,100 @@ static void assign_by_row(Sched *S, Ctx *C, Assign *A) {
   }
 }
 
+/* ---- flash-decode path (support_fd) ---- */
+static int64_t cur_block_cost(Assign *A) { /* metadata.py:766-775 */
+  if (A->cur_s2 < A->sc.cmp_s2_start) {
+    return A->cur_s2 == A->sc.cmp_s2_start - 1 ? A->sc.win_lbc : A->sc.win_nbc;
+  }
+  return A->cur_s2 == A->sc.s2_end - 1 ? A->sc.cmp_lbc : A->sc.cmp_nbc;
+}
+
+static void assign_by_block(Assign *A) { /* metadata.py:777-794 */
+  if (A->finished) return;
+  int64_t c = cur_block_cost(A);
+  int64_t guard = 0;
+  while (A->core_limit + fdiv(c, 2) >= A->core_cost + c) {
+    A->core_cost += c;
+    A->core_block += 1;
+    A->cur_s2 += 1;
+    A->bn2_cost -= c;
+    A->sc.s1g_cost -= c;
+    A->bn2_block -= 1;
+    A->sc.s1g_block -= 1;
+    c = cur_block_cost(A);
+    if (++guard > ROW_SCAN_CAP) return;
+  }
+}
+
+static void update_cursor(Sched *S, Ctx *C, Assign *A) { /* metadata.py:829-857 */
+  int upd_s1g = 0, upd_b = 0;
+  if (A->cur_s2 >= A->sc.s2_end) { A->cur_s2 = 0; A->cur_s1g += 1; upd_s1g = 1; }
+  if (A->cur_s1g >= C->s1g_base_num[A->cur_b]) { A->cur_s1g = 0; A->cur_bn2 += 1; }
+  if (A->cur_bn2 == S->batch * S->nkv) { A->cur_s1g = 0; A->cur_s2 = 0; A->finished = 1; return; }
+  if (fdiv(A->cur_bn2, S->nkv) != A->cur_b) { A->cur_b = fdiv(A->cur_bn2, S->nkv); A->cur_s1g = 0; upd_b = 1; upd_s1g = 1; }
+  if (upd_b) { batch_cache(S, A->cur_b, &A->bc); A->bn2_cost = C->bn2_cost[A->cur_b]; A->bn2_block = C->bn2_block[A->cur_b]; }
+  if (upd_s1g) { s1g_cache(S, A->cur_s1g, C, &A->bc, &A->sc); A->cur_s2 = A->sc.win_s2_start; }
+}
+
+static void force_assign(Sched *S, Ctx *C, Assign *A) { /* metadata.py:859-870 */
+  if (A->finished) return;
+  int64_t c = cur_block_cost(A);
+  A->core_cost += c;
+  A->core_block += 1;
+  A->cur_s2 += 1;
+  A->bn2_cost -= c;
+  A->bn2_block -= 1;
+  A->sc.s1g_cost -= c;
+  A->sc.s1g_block -= 1;
+  update_cursor(S, C, A);
+}
+
+typedef struct { /* FlashDecodeResult + the SplitResult FD fields, metadata.py:206-252 */
+  int64_t n_head, max_split, used_vec;
+  int64_t bn2[AIC_CORE_NUM + 64], m[AIC_CORE_NUM + 64], ws[AIC_CORE_NUM + 64], split[AIC_CORE_NUM + 64],
+      msize[AIC_CORE_NUM + 64];
+  int64_t idx[AIV_CORE_NUM + 64], m_start[AIV_CORE_NUM + 64], m_num[AIV_CORE_NUM + 64];
+} FdRes;
+
+static void record_fd(Sched *S, Ctx *C, Assign *A, const int64_t *bn2_end, const int64_t *g_s1_end,
+                      FdRes *F) { /* metadata.py:807-827 */
+  int64_t split_b = fdiv(bn2_end[A->cur_core - 1], S->nkv);
+  int64_t split_s1g = g_s1_end[A->cur_core - 1];
+  int64_t s1 = s1_size(S, split_b);
+  int64_t msz = split_s1g == C->s1g_base_num[split_b] - 1 ? s1 * S->group - split_s1g * S->m_base : S->m_base;
+  if (A->kv_split_part > F->max_split) F->max_split = A->kv_split_part;
+  int64_t h = F->n_head;
+  if (h >= S->aic) { S->err = 5; return; } /* the reference's lists hold aic entries */
+  F->bn2[h] = bn2_end[A->cur_core - 1];
+  F->m[h] = g_s1_end[A->cur_core - 1];
+  F->ws[h] = A->fd_data_num - A->kv_split_part;
+  F->split[h] = A->kv_split_part;
+  F->msize[h] = msz;
+  F->n_head += 1;
+}
+
+static void split_fd(Sched *S, FdRes *F) { /* metadata.py:925-954 */
+  int64_t total = 0;
+  for (int64_t i = 0; i < F->n_head; ++i) total += F->split[i] * F->msize[i];
+  if (S->aiv == 0) return;
+  int64_t avg = fdiv(total, S->aiv);
+  if (avg == 0) return;
+  int64_t cur = 0;
+  for (int64_t i = 0; i < F->n_head; ++i) {
+    int64_t nv = fdiv(F->split[i] * F->msize[i], avg);
+    if (nv == 0) continue;
+    int64_t ave = fdiv(F->msize[i], nv);
+    for (int64_t v = 0; v < nv; ++v) {
+      if (cur >= S->aiv) break; /* len(fd_idx) == aiv_core_num */
+      F->idx[cur] = i;
+      F->m_start[cur] = v * ave;
+      F->m_num[cur] = v < nv - 1 ? ave : F->msize[i] - v * ave;
+      cur += 1;
+    }
+  }
+  F->used_vec = cur;
+}
+
 int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
                     const int64_t *cu_q, int64_t n_cu_q,
                     const int64_t *cu_kv, int64_t n_cu_kv,
@@ -281,7 +380,7 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
                     int64_t batch, int64_t max_q, int64_t max_kv,
                     int64_t cmp_topk, int64_t cmp_ratio, int64_t mask_mode, int64_t win_left,
                     int64_t layout_q, int64_t layout_kv, int64_t has_cmp, int64_t aic,
-                    int32_t *out) {
+                    int64_t aiv, int64_t support_fd, int32_t *out) {
   Sched S;
   memset(&S, 0, sizeof(S));
   S.nq = nq; S.nkv = nkv; S.hd = hd;
@@ -290,6 +389,8 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
   S.batch = batch; S.max_q = max_q; S.max_kv = max_kv;
   S.cmp_topk = cmp_topk; S.cmp_ratio = cmp_ratio; S.mask_mode = mask_mode; S.win_left = win_left;
   S.layout_q = layout_q; S.layout_kv = layout_kv; S.has_cmp = has_cmp; S.aic = aic;
+  S.aiv = aiv; S.support_fd = support_fd;
+  if (aic > AIC_CORE_NUM + 64 || aiv > AIV_CORE_NUM + 64) return 1;
   memset(out, 0, sizeof(int32_t) * SAS_META_SIZE);
   params_init(&S);
   if (S.batch < 0 || S.aic < 0 || S.nkv <= 0 || S.group <= 0) return 1;
@@ -302,6 +403,8 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
   C.bn2_cost = mem + 4 * (B + 1); C.bn2_block = mem + 5 * (B + 1); C.bn2_lbc = mem + 6 * (B + 1);
   int64_t *bn2_end = mem + 7 * (B + 1), *g_s1_end = bn2_end + NC, *s2_end = g_s1_end + NC;
   int64_t used = 0;
+  FdRes F;
+  memset(&F, 0, sizeof(F));
 
   /* _calc_split_info */
   C.all_zero = 1;
@@ -337,6 +440,7 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
     used = 1;
     if (S.aic != 0) {
       Assign A; memset(&A, 0, sizeof(A));
+      A.kv_split_part = 1; A.fd_data_num = 1;
       int64_t max_cost = 0;
       A.unassigned = C.total_cost;
       A.bn2_cost = C.bn2_cost[0];
@@ -350,23 +454,37 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
         int64_t den = S.aic - A.cur_core; if (den < 1) den = 1;
         int64_t avg = fdiv(A.unassigned, den);
         A.core_cost = 0; A.core_block = 0;
-        A.core_limit = avg > C.max_s1g_cost ? avg : C.max_s1g_cost;
+        A.core_limit = S.support_fd ? avg : (avg > C.max_s1g_cost ? avg : C.max_s1g_cost);
         assign_by_batch(&S, &C, &A);
         if (S.err) break;
         assign_by_row(&S, &C, &A);
         if (S.err) break;
+        if (S.support_fd) {
+          assign_by_block(&A);
+          if (A.core_block == 0) force_assign(&S, &C, &A);
+          if (S.err) break;
+        }
         bn2_end[A.cur_core] = A.cur_bn2;
         g_s1_end[A.cur_core] = A.cur_s1g;
         s2_end[A.cur_core] = A.cur_s2;
         if (A.core_cost > max_cost) max_cost = A.core_cost;
         A.unassigned -= A.core_cost;
+        /* _is_need_record_fd (metadata.py:796-805) */
+        if (A.cur_core != 0 && A.kv_split_part > 1 &&
+            !(A.cur_bn2 == bn2_end[A.cur_core - 1] && A.cur_s1g == g_s1_end[A.cur_core - 1])) {
+          record_fd(&S, &C, &A, bn2_end, g_s1_end, &F);
+          if (S.err) break;
+          A.kv_split_part = 1;
+        }
+        if (A.sc.s2_start < A.cur_s2 && A.cur_s2 <= A.sc.s2_end) A.kv_split_part += 1;
       }
       used = A.cur_core + 1;
     }
+    if (F.n_head > 0) split_fd(&S, &F);
     if (used < 1) used = 1;
   }
   if (S.err) { free(mem); return S.err; }
-  /* _gen_metadata (the FD table stays zero: supportFd=False) */
+  /* _gen_metadata (first_fd_data_workspace_idx is never assigned: 0) */
   for (int64_t i = 0; i < AIC_CORE_NUM; ++i) {
     int32_t *row = out + i * FA_METADATA_SIZE;
     if (i >= used || i >= S.aic) { row[0] = 0; continue; }
@@ -378,6 +496,18 @@ int sas_meta_oracle(int64_t nq, int64_t nkv, int64_t hd,
     row[5] = (int32_t)g_s1_end[i];
     row[6] = (int32_t)s2_end[i];
     row[7] = 0;
+  }
+  for (int64_t i = 0; i < AIV_CORE_NUM; ++i) {
+    int32_t *row = out + AIC_CORE_NUM * FA_METADATA_SIZE + i * 8;
+    if (i >= F.used_vec || i >= S.aiv) { row[0] = 0; continue; }
+    int64_t f = F.idx[i];
+    row[0] = 1;
+    row[1] = (int32_t)F.bn2[f];
+    row[2] = (int32_t)F.m[f];
+    row[3] = (int32_t)F.ws[f];
+    row[4] = (int32_t)F.split[f];
+    row[5] = (int32_t)F.m_start[i];
+    row[6] = (int32_t)F.m_num[i];
   }
   free(mem);
   return 0;

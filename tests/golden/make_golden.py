@@ -15,6 +15,11 @@ Writes:
 
 * ``metadata_cases.npz`` -- ``configs`` (JSON list of keyword sets) and
   ``outputs`` (``int32[N, 1024]``) from ``metadata.sparse_attn_sharedkv_metadata``.
+* ``metadata_fd_cases.npz`` -- the same for the flash-decode schedule: the
+  reference scheduler class (``metadata._MetadataScheduler``) with its
+  ``supportFd`` attribute set to True before ``run()``; the configs add
+  ``aiv_core_num``. Configurations on which the reference's row walk does not
+  end within a time limit (its inner loop has no bound) are left out.
 * ``attn_cases.npz`` -- ``configs`` (JSON list of ``synth.make_case`` keyword
   sets plus index edits) and, per case ``i``, ``out_i`` (raw 16-bit pattern of
   the bf16/fp16 output, ``[T, H, D]``) and ``lse_i`` (``float32[T, H]``) from
@@ -164,7 +169,7 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of sparse_attn_sharedkv_tilelang")
     ap.add_argument("--n-random", type=int, default=1500)
-    ap.add_argument("--only", choices=["meta", "attn", "all"], default="all")
+    ap.add_argument("--only", choices=["meta", "fd", "attn", "all"], default="all")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     import golden as G  # reference
@@ -179,6 +184,43 @@ def main():
         np.savez_compressed(os.path.join(HERE, "metadata_cases.npz"), configs=np.array(json.dumps(cfgs)),
                             outputs=outs)
         print(f"metadata: {len(cfgs)} cases")
+
+    if args.only in ("fd", "all"):
+        import signal
+
+        rng = np.random.default_rng(20261202)
+        cand = metadata_configs(rng, 700)
+        for i, cfg in enumerate(cand):
+            cfg["aiv_core_num"] = int(rng.choice([48, 48, 72, 8, 1, 0]))
+        # decode-shaped batches with few cores, where rows are cut between cores
+        for B, kv, aic in [(1, 70000, 24), (2, 200000, 24), (4, 9000, 24), (3, 130000, 36), (1, 8193, 8)]:
+            cand.append(dict(num_heads_q=64, num_heads_kv=1, head_dim=512, cu_seqlens_q=list(range(B + 1)),
+                             seqused_kv=[kv + 977 * j for j in range(B)], batch_size=B, max_seqlen_q=1,
+                             max_seqlen_kv=kv + 977 * B, layout_q="TND", has_cmp_kv=True, cmp_ratio=4,
+                             cmp_topk=1024, aic_core_num=aic, aiv_core_num=48))
+
+        def on_alarm(*_):
+            raise TimeoutError
+
+        signal.signal(signal.SIGALRM, on_alarm)
+        keep, outs = [], []
+        for cfg in cand:
+            kw = _to_torch_kwargs(cfg)
+            sched = M._MetadataScheduler(**kw)
+            sched.supportFd = True
+            signal.alarm(5)
+            try:
+                o = sched.run().numpy()
+            except (TimeoutError, IndexError):
+                continue
+            finally:
+                signal.alarm(0)
+            keep.append(cfg)
+            outs.append(o)
+        np.savez_compressed(os.path.join(HERE, "metadata_fd_cases.npz"), configs=np.array(json.dumps(keep)),
+                            outputs=np.stack(outs).astype(np.int32))
+        n_fd = int(sum((o[36 * 8:36 * 8 + 72 * 8].reshape(72, 8)[:, 0] != 0).any() for o in outs))
+        print(f"metadata fd: {len(keep)} of {len(cand)} cases ({n_fd} with flash-decode rows)")
 
     if args.only in ("attn", "all"):
         arrays = {}

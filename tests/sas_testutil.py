@@ -187,3 +187,9 @@ def oracle_sampled(d, tokens, dtype="bf16", win_left=127):
         outs.append(o)
         lses.append(l)
     return np.stack(outs), np.stack(lses)
+
+
+def load_meta_fd_fixtures():
+    """Flash-decode schedules from the reference scheduler with supportFd on."""
+    z = np.load(os.path.join(GOLDEN, "metadata_fd_cases.npz"))
+    return json.loads(str(z["configs"])), z["outputs"]

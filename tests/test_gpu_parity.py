@@ -248,3 +248,60 @@ def test_metadata_default_returns_cpu_tensor():
     a = sparse_attn_sharedkv_metadata(**kw)
     b = sparse_attn_sharedkv_metadata(device="cuda", **kw)
     assert a.device.type == "cpu" and b.is_cuda and torch.equal(a, b.cpu())
+
+
+def _meta_gpu_fd(cfg):
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
+
+    kw = dict(cfg)
+    for k in ("cu_seqlens_q", "seqused_kv"):
+        if k in kw:
+            kw[k] = torch.tensor(kw[k], dtype=torch.int32)
+    return sparse_attn_sharedkv_metadata(device="cuda", support_fd=True, **kw).cpu().numpy()
+
+
+def test_metadata_fd_gpu_bit_exact_vs_reference_fixtures():
+    cfgs, outs = U.load_meta_fd_fixtures()
+    bad = [i for i, c in enumerate(cfgs) if not np.array_equal(_meta_gpu_fd(c), outs[i])]
+    assert not bad, f"{len(bad)} mismatches, first {bad[:5]}: {[cfgs[i] for i in bad[:2]]}"
+
+
+def test_metadata_fd_gpu_fuzz_vs_oracle():
+    from oracle import meta_oracle as M
+
+    rng = np.random.default_rng(8)
+    bad = []
+    for it in range(150):
+        B = int(rng.integers(1, 40))
+        ql = rng.integers(1, rng.choice([2, 3, 50, 600]), size=B)
+        kv = np.maximum(rng.integers(1, rng.choice([300, 5000, 200000]), size=B), ql)
+        cfg = dict(num_heads_q=int(rng.choice([16, 64, 128])), num_heads_kv=1, head_dim=512,
+                   cu_seqlens_q=[0] + np.cumsum(ql).tolist(), seqused_kv=kv.tolist(), batch_size=B,
+                   max_seqlen_q=int(ql.max()), max_seqlen_kv=int(kv.max()), layout_q="TND",
+                   has_cmp_kv=bool(rng.random() < 0.8), cmp_ratio=int(rng.choice([4, 128])),
+                   cmp_topk=int(rng.choice([0, 256, 512, 1024])), aic_core_num=int(rng.choice([24, 36, 8])),
+                   aiv_core_num=int(rng.choice([48, 72, 8])))
+        if not np.array_equal(_meta_gpu_fd(cfg), M.metadata(support_fd=True, **cfg)):
+            bad.append(cfg)
+    assert not bad, f"{len(bad)} mismatches; first {json.dumps(bad[0])[:400]}"
+
+
+@pytest.mark.parametrize("cfg", [
+    dict(ctx=[70000, 9000, 200000, 130], q_lens=[1, 1, 1, 1], H=64, K=1024, seed=43),   # rows cut between cores
+    dict(ctx=[3000, 900], q_lens=[400, 300], H=64, K=256, seed=44),                     # plan kernel
+], ids=["decode", "prefill"])
+def test_attention_accepts_flash_decode_schedule(cfg):
+    """A flash-decode schedule covers the same tokens (a row cut between two
+    cores belongs to the core that starts with it, kernel.py:254-278), so the
+    forward gives the same bits with either schedule."""
+    from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
+
+    case = U.build_case(cfg)
+    out, lse = U.run_api(case)
+    cu = torch.tensor(np.asarray(case.cu_seqlens_q), dtype=torch.int32)
+    md = sparse_attn_sharedkv_metadata(
+        num_heads_q=case.H, num_heads_kv=1, head_dim=512, cu_seqlens_q=cu,
+        seqused_kv=torch.tensor(case.seqused_kv, dtype=torch.int32), batch_size=len(cu) - 1, layout_q="TND",
+        cmp_topk=case.K, cmp_ratio=case.cmp_ratio, device="cuda", support_fd=True)
+    out2, lse2 = U.run_api(case, metadata=md)
+    assert np.array_equal(out2, out) and np.array_equal(lse2, lse)

@@ -142,3 +142,16 @@ def test_sampled_oracle_matches_full_oracle():
                        seqused_kv=d["seqused_kv"].numpy(), sinks=d["sinks"].numpy(),
                        softmax_scale=d["softmax_scale"], cmp_ratio=4, tokens=toks)
     assert np.array_equal(so, fo[toks]) and np.array_equal(sl, fl[toks])
+
+
+def test_meta_oracle_flash_decode_matches_reference_fixtures():
+    """The flash-decode branches (metadata.py:777-870, 925-954), pinned by the
+    reference scheduler run with supportFd on (tests/golden/make_golden.py)."""
+    import sas_testutil as U
+    from oracle import meta_oracle as M
+
+    cfgs, outs = U.load_meta_fd_fixtures()
+    n_fd = sum(int((o[288:288 + 576].reshape(72, 8)[:, 0] != 0).any()) for o in outs)
+    assert len(cfgs) > 500 and n_fd > 100
+    bad = [i for i, c in enumerate(cfgs) if not np.array_equal(M.metadata(support_fd=True, **c), outs[i])]
+    assert not bad, bad[:5]

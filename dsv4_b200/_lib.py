@@ -49,6 +49,10 @@ EXPORTS = {
                       i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
     "sas_metadata_fd": ([vp, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
                          i32, i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
+    "sas_sparse_attn_sharedkv_bwd": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp,
+                                      i32, vp, i64, i32, vp, i32, vp, i32, vp, f32, i32, i32, i32, vp, vp, vp, vp,
+                                      vp, vp], ctypes.c_int),
+    "sas_bwd_cast": ([vp, vp, i64, i32, vp], ctypes.c_int),
     "sas_fwd_workspace_bytes": ([i32, i32, i32], sz),
     "sas_fwd_set_option": ([i32, ctypes.c_double, vp], ctypes.c_int),
     "sas_sparse_attn_sharedkv_fwd": ([vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp, i32, vp, i64,

@@ -184,6 +184,32 @@ int sas_sparse_attn_sharedkv_fwd(
     void* stream);
 
 /* ------------------------------------------------------------------------
+ * Backward, consuming the forward's LSE. The reference documents the LSE as
+ * the input of a FlashAttention-2 style backward
+ * (sparse_attn_sharedkv_tilelang/api.py:32-35, 176-184) and ships none; this
+ * is the gradient of the forward's math (golden.py:69-204, exact softmax with
+ * the sink in the denominator) for every query token:
+ *   dq [num_tokens, num_heads, 512] (q's type), written;
+ *   d_ori_kv / d_cmp_kv fp32, shaped like the pools, ACCUMULATED into (zero
+ *     them first; K = V, so a row gets its key and value gradients);
+ *   d_sinks fp32 [num_heads], accumulated into.
+ * dout, q and out are [num_tokens, num_heads, 512] in the I/O type, lse fp32
+ * [num_tokens, num_heads] as the forward returned it. The other arguments
+ * are the forward's. sas_bwd_cast converts n fp32 values to the I/O type
+ * (dtype code), e.g. a pool gradient.
+ * ---------------------------------------------------------------------- */
+int sas_sparse_attn_sharedkv_bwd(
+    const void* dout, const void* q, const void* out, const float* lse, int32_t num_tokens, int32_t num_heads,
+    int32_t head_dim, int32_t dtype, int32_t layout_q, int32_t batch, int32_t max_seqlen_q,
+    const int32_t* cu_seqlens_q, const int32_t* seqused_kv, const void* ori_kv, int64_t ori_num_blocks,
+    int32_t ori_block_size, const int32_t* ori_block_table, int32_t ori_table_stride, const void* cmp_kv,
+    int64_t cmp_num_blocks, int32_t cmp_block_size, const int32_t* cmp_block_table, int32_t cmp_table_stride,
+    const int32_t* cmp_sparse_indices, int32_t topk, const float* sinks, float softmax_scale, int32_t cmp_ratio,
+    int32_t ori_win_left, int32_t scenario, void* dq, float* d_ori_kv, float* d_cmp_kv, float* d_sinks,
+    int32_t* status, void* stream);
+int sas_bwd_cast(const float* src, void* dst, int64_t n, int32_t dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Process-wide options of the forward kernel (no counterpart in the
  * reference, whose knobs are compile-time JIT parameters, api.py:59-126).
  *   SAS_OPT_RESCALE_THRESHOLD (value): the online softmax keeps a per-head

@@ -69,6 +69,8 @@ def parse():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--max-requests", type=int, default=0,
+                    help="keep only the first N requests of this rank's share (small cases for ncu captures)")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3)
     return a
@@ -500,6 +502,8 @@ def ours_arm(a, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     ctx, ql, H, K, bs, scaling = workload(a.config, rank, world, a.mode)
+    if a.max_requests > 0:
+        ctx, ql = ctx[:a.max_requests], ql[:a.max_requests]
     heads = a.mode == "heads"
     d = synth.make_case_torch(ctx=ctx, q_lens=ql, H=H, K=K, bs=bs, seed=1000 if heads else 1000 + rank, device=dev)
     q = d.pop("q")
@@ -639,7 +643,9 @@ def ours_arm(a, rank, world, local_rank):
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": total_ms / a.steps, "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
         "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": a.config + ": " + describe(a.config, world), "tokens_per_gpu": T, "heads": H,
+        "config": {"workload": a.config + ": " + describe(a.config, world)
+                   + (f" (first {a.max_requests} requests only)" if a.max_requests > 0 else ""),
+                   "tokens_per_gpu": T, "heads": H,
                    "topk": K, "head_dim": 512, "window": 128, "cmp_ratio": 4, "block": bs,
                    "l2": "flushed (512 MB write) between timed steps", "graph": graph is not None,
                    "parallelism": (f"head-sharded x{world} ({H // world} heads/GPU, NCCL all-gather)" if heads

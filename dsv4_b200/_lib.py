@@ -20,7 +20,7 @@ LIB_PATH = os.path.join(_HERE, "libsas_b200.so")
 SAS_OK = 0
 STAGE_PLAN, STAGE_ATTENTION, STAGE_COMBINE, STAGE_ALL = 1, 2, 4, 7
 FLAG_AFTER_METADATA = 8  # the preceding kernel on the stream is sas_metadata for the same call
-OPT_RESCALE_THRESHOLD, OPT_TRACE_BUFFER, OPT_SPLIT_TOKENS, OPT_WAIT_LIMIT_NS, OPT_SCHED_SCAN_CAP, OPT_DECODE_KERNEL = 1, 2, 3, 4, 5, 6
+OPT_RESCALE_THRESHOLD, OPT_TRACE_BUFFER, OPT_SPLIT_TOKENS, OPT_WAIT_LIMIT_NS, OPT_SCHED_SCAN_CAP = 1, 2, 3, 4, 5
 ERRORS = {
     1: "invalid argument",
     2: "unsupported configuration",

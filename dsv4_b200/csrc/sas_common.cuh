@@ -134,82 +134,6 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
-// ---------------------------------------------------------------- cluster
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cluster_id_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t nclusters_x() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-// Address in the shared::cluster window of CTA `rank`'s copy of the local
-// shared-memory address `saddr`.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-// Arrive (release, cluster scope) on an mbarrier of a CTA of the cluster.
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t remote_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote_bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_test_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait (as mbar_wait) for arrivals that other CTAs of the cluster
-// release at cluster scope.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, volatile CtaCtl* ctl, int* status,
-                                                  int where) {
-  const uint64_t lim = ctl->limit_ns;
-  const uint64_t t0 = globaltimer();
-  uint32_t n = 0;
-  while (!(lim < kPollLimitNs ? mbar_test_wait_cluster(bar, parity) : mbar_try_wait_cluster(bar, parity))) {
-    if (lim < kPollLimitNs || (++n & 63u) == 0) {
-      if (ctl->abort) return false;
-      if (globaltimer() - t0 > lim) {
-        ctl->abort = 1;
-        if (status) atomicCAS(status, 0, SAS_ERR_TIMEOUT_BASE + where);
-        return false;
-      }
-    }
-  }
-  return true;
-}
-// Cluster-wide execution barrier (every thread of every CTA of the cluster).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
 // ------------------------------------------------------------------- TMA
 // Programmatic dependent launch: a kernel launched with the programmatic
 // stream-serialization attribute may start before the previous kernel on the

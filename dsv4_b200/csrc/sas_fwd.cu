@@ -1863,27 +1863,8 @@ size_t g_trace_bytes = 0;  // size of the trace buffer
 int g_trace_dev = -1;      // the device that owns it
 unsigned long long g_wait_ns = SAS_WAIT_LIMIT_NS;
 
-}  // namespace
-
-namespace sas {
-size_t dec_workspace_bytes(int num_sms);
-int launch_cluster_decode(const CUtensorMap& tm_q, int dtype, int T, int H, int B, int S, int layout, int scenario,
-                          int K, int ratio, int win_left, int ori_bs, int ori_bt_stride, int cmp_bs,
-                          int cmp_bt_stride, int ori_nblk, int cmp_nblk, const void* ori_kv, const void* cmp_kv,
-                          const int32_t* ori_bt, const int32_t* cmp_bt, const int32_t* idx, const int32_t* cu,
-                          const int32_t* seqused_kv, const int32_t* meta, const float* sinks, float scale_log2,
-                          void* out, float* lse, void* ws, int num_sms, int32_t* status, int q_box_h, bool early,
-                          unsigned long long wait_ns, cudaStream_t st);
-}  // namespace sas
-
-namespace {
-
-// Cluster decode kernel (csrc/sas_dec.cu): 0 never, 1 for batches of at most
-// kFusedMaxT query tokens with a window of at most 128 rows.
-int g_decode_kernel = 0;
-
 struct WsLayout {
-  size_t tok, unit, po, pl, cnt, dec, total;
+  size_t tok, unit, po, pl, cnt, total;
 };
 WsLayout ws_layout(int T, int H, int num_sms) {
   const int G = (H + HG - 1) / HG;
@@ -1894,8 +1875,7 @@ WsLayout ws_layout(int T, int H, int num_sms) {
   w.po = align_up(w.unit + sizeof(int32_t) * ((size_t)T + 1), 256);
   w.pl = align_up(w.po + sizeof(float) * (size_t)R * 2 * G * HG * D, 256);
   w.cnt = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
-  w.dec = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
-  w.total = align_up(w.dec + sas::dec_workspace_bytes(num_sms), 256);
+  w.total = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
   return w;
 }
 
@@ -1936,10 +1916,6 @@ extern "C" int sas_fwd_set_option(int32_t option, double value, void* ptr) {
     case SAS_OPT_SCHED_SCAN_CAP:
       if (!(value >= 0.0 && value <= 4e18)) return SAS_ERR_INVALID_ARG;
       sas::set_sched_scan_cap((long long)value);
-      return SAS_OK;
-    case SAS_OPT_DECODE_KERNEL:
-      if (!(value == 0.0 || value == 1.0)) return SAS_ERR_INVALID_ARG;
-      g_decode_kernel = (int)value;
       return SAS_OK;
     case SAS_OPT_SPLIT_TOKENS:
       if (!(value >= -1.0 && value <= 1e6)) return SAS_ERR_INVALID_ARG;
@@ -2020,23 +1996,6 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
 
-  // decode batches: the cluster kernel (no plan, no split tokens, no trace)
-  const bool use_dec = g_decode_kernel == 1 && fused && n_win_chunks == 1 && g_trace == nullptr && g_cut_cost < 0 &&
-                       g_tau == 0.0f;
-  if (use_dec) {
-    if (!(stage_mask & SAS_STAGE_ATTENTION)) return SAS_OK;
-    alignas(64) CUtensorMap tmq;
-    const CUtensorMapDataType tdt2 = dtype == SAS_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    if (!make_q_map(&tmq, q, num_tokens, num_heads, std::min(HG, num_heads), tdt2)) return SAS_ERR_CUDA;
-    return sas::launch_cluster_decode(
-        tmq, dtype, num_tokens, num_heads, batch, max_seqlen_q, layout_q, scenario, scenario == 3 ? topk : 0,
-        scenario >= 2 ? cmp_ratio : 1, ori_win_left, ori_block_size, ori_table_stride,
-        scenario >= 2 ? cmp_block_size : 1, cmp_table_stride, (int)ori_num_blocks,
-        (int)(scenario >= 2 ? cmp_num_blocks : ori_num_blocks), ori_kv, scenario >= 2 ? cmp_kv : ori_kv,
-        ori_block_table, cmp_block_table, cmp_sparse_indices, cu_seqlens_q, seqused_kv, metadata, sinks,
-        softmax_scale * kLog2e, out, lse, ws + wl.dec, num_sms, status, std::min(HG, num_heads), early, g_wait_ns, st);
-  }
   if ((stage_mask & SAS_STAGE_PLAN) && !fused) {
     if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }

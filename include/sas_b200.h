@@ -237,11 +237,6 @@ int sas_bwd_cast(const float* src, void* dst, int64_t n, int32_t dtype, void* st
  *   SAS_OPT_SCHED_SCAN_CAP (value): rows the scheduler's greedy walk may scan
  *     for one core before it stops and records SAS_ERR_SCHED_OVERRUN (0
  *     restores the default of 2^24).
- *   SAS_OPT_DECODE_KERNEL (value): 1 (default) runs batches of at most 512
- *     query tokens whose window is at most 128 rows on the cluster decode
- *     kernel (four CTAs share each token's tiles and exchange tile maxima, so
- *     every KV row is copied once); 0 always uses the tiled kernel. The two
- *     round P at the same points; their fp32 sums differ in order.
  * These options are process-wide and not synchronised: set them while no
  * other host thread is launching through this library. The trace buffer is
  * one pointer for every device; it must hold 46 uint64 per CTA of the grid.
@@ -251,7 +246,6 @@ int sas_bwd_cast(const float* src, void* dst, int64_t n, int32_t dtype, void* st
 #define SAS_OPT_SPLIT_TOKENS 3
 #define SAS_OPT_WAIT_LIMIT_NS 4
 #define SAS_OPT_SCHED_SCAN_CAP 5
-#define SAS_OPT_DECODE_KERNEL 6
 int sas_fwd_set_option(int32_t option, double value, void* ptr);
 
 #ifdef __cplusplus

@@ -64,20 +64,8 @@ def test_metadata_gpu_fuzz_vs_oracle():
     assert not bad, f"{len(bad)} mismatches; first {json.dumps(bad[0])[:400]}"
 
 
-@pytest.fixture(params=["cluster", "tiled"])
-def kernel(request):
-    """Run a test on the cluster decode kernel (the default for batches of at
-    most 512 tokens) and on the tiled kernel (SAS_OPT_DECODE_KERNEL = 0)."""
-    from dsv4_b200 import _lib as L
-
-    L.check(L.lib().sas_fwd_set_option(L.OPT_DECODE_KERNEL, 1.0 if request.param == "cluster" else 0.0, None),
-            "set_option")
-    yield request.param
-    L.check(L.lib().sas_fwd_set_option(L.OPT_DECODE_KERNEL, 1.0, None), "set_option")
-
-
 @pytest.mark.parametrize("i", range(9))
-def test_attention_vs_reference_fixtures(i, kernel):
+def test_attention_vs_reference_fixtures(i):
     cfg, ref_out, ref_lse = U.load_attn_fixtures()[i]
     case = U.build_case(cfg)
     out, lse = U.run_api(case)
@@ -98,7 +86,7 @@ RANDOM_CASES = [
 
 
 @pytest.mark.parametrize("cfg", RANDOM_CASES, ids=[f"r{i}" for i in range(len(RANDOM_CASES))])
-def test_attention_vs_oracle(cfg, kernel):
+def test_attention_vs_oracle(cfg):
     case = U.build_case(cfg)
     out, lse = U.run_api(case)
     ro, rl = U.oracle_forward(case)
@@ -106,7 +94,7 @@ def test_attention_vs_oracle(cfg, kernel):
     U.check_result_ref(out, ro, case.dtype)
 
 
-def test_attention_c2_scale_sampled(kernel):
+def test_attention_c2_scale_sampled():
     """BASELINE config 2 shapes (B=64, H=64, K=512, ctx U[8k,64k], block 128),
     checked against the oracle on a sample of 8 requests."""
     from dsv4_b200 import synth
@@ -188,7 +176,7 @@ def _covered_tokens(md, cu):
     dict(ctx=[3000, 5000, 800, 12000], q_lens=[1, 2, 1, 3], H=64, K=512, seed=41),  # plan in the attention kernel
     dict(ctx=[3000, 900], q_lens=[400, 300], H=64, K=256, seed=42),                 # plan kernel
 ], ids=["fused_plan", "plan_kernel"])
-def test_uncovered_tokens_are_zero(cfg, kernel):
+def test_uncovered_tokens_are_zero(cfg):
     """Metadata with a core disabled: the tokens of its window get zero output
     and LSE, every other token is unchanged."""
     from dsv4_b200.metadata import sparse_attn_sharedkv_metadata
@@ -229,7 +217,7 @@ def test_bsnd_layout_and_return_types():
     assert torch.equal(l_b.reshape(B * S, 64), l_tnd)
 
 
-def test_bsnd_padding_rows_are_zero(kernel):
+def test_bsnd_padding_rows_are_zero():
     from dsv4_b200 import sparse_attn_sharedkv
 
     case = U.build_case(dict(ctx=[900, 1200], q_lens=[4, 4], H=64, K=256, seed=32))
@@ -243,7 +231,7 @@ def test_bsnd_padding_rows_are_zero(kernel):
     assert torch.count_nonzero(o[0, :2]) > 0
 
 
-def test_deterministic_replay(kernel):
+def test_deterministic_replay():
     case = U.build_case(dict(ctx=[20000, 30000, 5000], q_lens=[1, 2, 1], H=128, K=512, seed=41))
     a, la = U.run_api(case)
     b, lb = U.run_api(case)

@@ -156,13 +156,18 @@ KERNEL_SOURCES = ("dsv4_b200/csrc/sas_fwd.cu", "dsv4_b200/csrc/sas_common.cuh")
 
 
 def kernel_source_sha256() -> str:
-    """Hash of the attention kernel's sources, stamped into every profile summary."""
+    """Hash of the attention kernel's sources, stamped into every profile
+    summary. Comment-only lines and blank lines are left out, so editing a
+    comment does not retire a profile."""
     import hashlib
 
     h = hashlib.sha256()
     for f in KERNEL_SOURCES:
-        with open(os.path.join(ROOT, f), "rb") as fh:
-            h.update(fh.read())
+        with open(os.path.join(ROOT, f)) as fh:
+            for line in fh:
+                code = line.strip()
+                if code and not code.startswith("//"):
+                    h.update(code.encode() + b"\n")
     return h.hexdigest()[:16]
 
 

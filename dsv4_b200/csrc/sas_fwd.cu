@@ -1377,9 +1377,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == kCoordWarp) {
     // =============================== row resolution, up to CD chunks ahead
     // Lane l resolves rows l, l+32, l+64, l+96 of every chunk through the
-    // block tables (kernel.py:285-401, 686-766), writes the pool row (or -1)
-    // and the validity mask into the ring, and starts each valid row on its
-    // way into L2, so the loaders' copies later hit L2.
+    // block tables (kernel.py:285-401, 686-766) and writes the pool row (or
+    // -1) and the validity mask into the ring.
     // A whole tile (up to 4 chunks) is resolved per round with all its loads
     // in flight together: the index rows, then the block-table entries.
     TileIter it;

@@ -21,8 +21,11 @@ Workloads (synthetic N(0,1) data, seeded):
       (per GPU, weak scaling).
 
 --mode heads (with any config): the head-sharded variant. Every rank holds
-every request and computes H/N heads; the outputs and LSEs are all-gathered
-with NCCL (dsv4_b200/sharding.py). Strong scaling; KV is read by every GPU.
+every request and computes H/N heads; with --gather p2p (default) the
+attention kernel stores each result into every rank's output buffer through
+peer pointers into symmetric memory, with --gather nccl an NCCL all-gather
+follows the kernel (dsv4_b200/sharding.py). Strong scaling; KV is read by
+every GPU.
 
 The JSON line carries: value (query tokens/s, whole job), ms_per_step,
 roofline of the dominant kernel (the attention kernel alone, timed live with
@@ -65,6 +68,9 @@ def parse():
     ap.add_argument("--mode", default="requests", choices=["requests", "heads"],
                     help="requests: each rank runs its own requests (no collective); heads: every rank runs "
                          "H/N heads of all requests and the outputs are all-gathered over NCCL")
+    ap.add_argument("--gather", default="p2p", choices=["p2p", "nccl"],
+                    help="head-sharded mode: the attention kernel stores every result into all ranks' outputs "
+                         "through peer pointers (p2p), or the kernel runs and an NCCL all-gather follows (nccl)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -519,12 +525,13 @@ def ours_arm(a, rank, world, local_rank):
     flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    from dsv4_b200.sharding import head_sharded_forward, head_range
+    from dsv4_b200.sharding import head_sharded_forward, head_sharded_forward_p2p, head_range
 
     h0, h1 = head_range(H, world, rank) if heads else (0, H)
+    hs_fwd = head_sharded_forward_p2p if a.gather == "p2p" else head_sharded_forward
     if heads and world > 1:
         def step():
-            o, l = head_sharded_forward(q, **dict(d))
+            o, l = hs_fwd(q, **dict(d))
             out.copy_(o)
             lse.copy_(l)
     else:
@@ -620,7 +627,7 @@ def ours_arm(a, rank, world, local_rank):
     # step i+1's inputs go up while step i computes and step i-1's results come
     # down (two device buffer sets). The window of K steps is timed whole.
     e2e_ms, h2d, d2h, e2e_note = e2e_pipelined(a, d, q, heads, world, dev, sparse_attn_sharedkv,
-                                               head_sharded_forward, stream)
+                                               hs_fwd, stream)
 
     # max over ranks
     t = torch.tensor([total_ms, e2e_ms, attn_ms], dtype=torch.float64, device=dev)
@@ -653,8 +660,9 @@ def ours_arm(a, rank, world, local_rank):
                    "tokens_per_gpu": T, "heads": H,
                    "topk": K, "head_dim": 512, "window": 128, "cmp_ratio": 4, "block": bs,
                    "l2": "flushed (512 MB write) between timed steps", "graph": graph is not None,
-                   "parallelism": (f"head-sharded x{world} ({H // world} heads/GPU, NCCL all-gather)" if heads
-                                   else f"request-parallel x{world}")},
+                   "parallelism": ((f"head-sharded x{world} ({H // world} heads/GPU, " +
+                                    ("gathered by the kernel's peer stores)" if a.gather == "p2p"
+                                     else "NCCL all-gather)")) if heads else f"request-parallel x{world}")},
         "us_per_layer": total_ms / a.steps * 1e3,
         "attention_kernel_us": attn_ms * 1e3,
         "hbm_gbs_attention": achieved,

@@ -49,6 +49,9 @@ EXPORTS = {
                       i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
     "sas_metadata_fd": ([vp, i32, vp, i32, vp, i32, vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32,
                          i32, i32, i32, i32, vp, vp, vp, sz, vp], ctypes.c_int),
+    "sas_sparse_attn_sharedkv_fwd_gather": ([vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp, i32, vp,
+                                             i64, i32, vp, i32, vp, i32, vp, vp, f32, i32, i32, i32, vp, vp, i32,
+                                             i32, i32, i32, i32, vp, vp, sz, vp], ctypes.c_int),
     "sas_sparse_attn_sharedkv_bwd": ([vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i32, vp,
                                       i32, vp, i64, i32, vp, i32, vp, i32, vp, f32, i32, i32, i32, vp, vp, vp, vp,
                                       vp, vp], ctypes.c_int),

@@ -24,6 +24,7 @@ api.py:279-282): N2 = 1, D = 512, N1 a multiple of 8, bf16 or fp16.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Tuple, Union
 
 import torch
@@ -74,12 +75,18 @@ def sparse_attn_sharedkv(
     out: Optional[torch.Tensor] = None,
     lse_out: Optional[torch.Tensor] = None,
     _stages: int = _lib.STAGE_ALL,
+    _gather=None,
 ) -> Union[torch.Tensor, Tuple[torch.Tensor, torch.Tensor]]:
     """Forward pass; returns ``attention_out`` with the layout of ``q``.
 
     ``out`` / ``lse_out`` optionally supply preallocated result buffers
     (same shapes as the returned tensors), which CUDA-graph capture wants.
     ``seqused_q`` is accepted for API parity and unused (api.py:186).
+    ``_gather`` (internal, ``dsv4_b200.sharding``) is ``(out_ptrs, lse_ptrs,
+    heads_total, head_offset)``: the call computes heads ``[head_offset,
+    head_offset + N1)`` and writes them into every buffer of ``out_ptrs`` /
+    ``lse_ptrs`` (one per rank, outputs of ``heads_total`` heads); nothing is
+    returned.
     """
     del seqused_q
     assert ori_mask_mode == 4, "only ori_mask_mode=4 supported"
@@ -178,15 +185,34 @@ def sparse_attn_sharedkv(
         metadata = sparse_attn_sharedkv_metadata(**meta_kwargs)
         # nothing is enqueued between it and the attention launch, which may
         # then overlap it
-        flags = _lib.FLAG_AFTER_METADATA
+        flags = _lib.FLAG_AFTER_METADATA if _gather is None else 0
     md = metadata.to(device=dev, dtype=torch.int32)
     assert md.numel() == SAS_META_SIZE, f"metadata must have {SAS_META_SIZE} int32 entries (got {md.numel()})"
     md = md.reshape(SAS_META_SIZE).contiguous()
 
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if _gather is not None:
+        out_ptrs, lse_ptrs, heads_total, head_offset = _gather
+        n = len(out_ptrs)
+        optrs = (ctypes.c_void_p * n)(*out_ptrs)
+        lptrs = (ctypes.c_void_p * n)(*lse_ptrs)
+        rc = lib.sas_sparse_attn_sharedkv_fwd_gather(
+            q_flat.data_ptr(), T1, N1, D, dcode, 1 if layout_q == "TND" else 0, int(B), int(S), _lib.ptr(cu),
+            skv.data_ptr(),
+            ori_kv_dev.data_ptr(), ori_kv_dev.shape[0], ori_kv_dev.shape[1], ori_bt.data_ptr(), ori_bt.shape[1],
+            _lib.ptr(cmp_kv_dev), cmp_kv_dev.shape[0] if cmp_kv_dev is not None else 0,
+            cmp_kv_dev.shape[1] if cmp_kv_dev is not None else 0, _lib.ptr(cmp_bt),
+            cmp_bt.shape[1] if cmp_bt is not None else 0,
+            _lib.ptr(idx_dev), int(K), sinks_dev.data_ptr(), md.data_ptr(), float(softmax_scale),
+            int(cmp_ratio_eff), int(ori_win_left), scenario, optrs, lptrs, n, int(heads_total), int(head_offset),
+            st.num_sms, int(_stages), st.status.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+        if rc in (1, 2):
+            raise ValueError(f"sparse_attn_sharedkv: {_lib.ERRORS[rc]}")
+        _lib.check(rc, "sas_sparse_attn_sharedkv_fwd_gather")
+        return None
     out_flat = out.view(T1, N1, D) if out is not None else torch.empty((T1, N1, D), dtype=q.dtype, device=dev)
     lse_flat = lse_out.view(T1, N1) if lse_out is not None else torch.empty((T1, N1), dtype=torch.float32,
                                                                               device=dev)
-    stream = torch.cuda.current_stream(dev).cuda_stream
     rc = lib.sas_sparse_attn_sharedkv_fwd(
         q_flat.data_ptr(), T1, N1, D, dcode, 1 if layout_q == "TND" else 0, int(B), int(S), _lib.ptr(cu),
         skv.data_ptr(),

@@ -164,6 +164,41 @@ struct TokInfo {
   int b, s_g, n_cmp, thr;
 };
 
+// Where a call's results go. Normally one output [T, H, 512] and one LSE
+// [T, H]. The head-sharded multi-GPU forward computes heads [h0, h0 + H) of
+// outputs that hold H_total heads per token, and writes every result into
+// the output buffers of all n ranks (peer pointers into symmetric memory), so
+// the outputs are gathered as they are produced and no all-gather follows.
+constexpr int kMaxOut = 8;
+struct OutDesc {
+  uint8_t* out[kMaxOut];
+  float* lse[kMaxOut];  // lse[0] == nullptr: no LSE
+  int n, H_total, h0;
+  __device__ __forceinline__ size_t row(int t, int hh) const { return (size_t)t * H_total + h0 + hh; }
+  __device__ __forceinline__ void st32(int t, int hh, int col, uint32_t w) const {
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint32_t*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+  }
+  __device__ __forceinline__ void st64(int t, int hh, int col, uint2 w) const {
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint2*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+  }
+  __device__ __forceinline__ void st16(int t, int hh, int col, uint16_t w) const {
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint16_t*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+  }
+  __device__ __forceinline__ void lse_st(int t, int hh, float v) const {
+    if (lse[0])
+      for (int k = 0; k < n; ++k) lse[k][row(t, hh)] = v;
+  }
+  // zero the H heads of token t, threads [i0, i0 + stride) of the caller
+  __device__ __forceinline__ void zero_token(int t, int H, int i0, int stride) const {
+    for (int k = 0; k < n; ++k) {
+      uint4* o = reinterpret_cast<uint4*>(out[k] + row(t, 0) * D * 2);
+      for (int i = i0; i < H * D * 2 / 16; i += stride) o[i] = make_uint4(0, 0, 0, 0);
+      if (lse[0])
+        for (int h = i0; h < H; h += stride) lse[k][row(t, h)] = 0.f;
+    }
+  }
+};
+
 struct PlanParams {
   int T, B, S, layout, scenario, K, ratio, win_left, n_win_chunks;
   const int32_t* cu;
@@ -171,9 +206,8 @@ struct PlanParams {
   const int32_t* meta;
   TokInfo* tok;
   int32_t* unit_start;  // [T+1]
-  int H, dtype_bytes;
-  void* out;            // rows of tokens without work are zeroed here
-  float* lse;
+  int H;
+  OutDesc od;           // rows of tokens without work are zeroed here
   int32_t* merge_cnt;   // [n_cnt] split-token arrival counters, zeroed here
   int n_cnt;
 };
@@ -189,8 +223,7 @@ struct FwdParams {
   const int32_t* idx;
   const float* sinks;
   float scale_log2;
-  void* out;
-  float* lse;
+  OutDesc od;
   const TokInfo* tok;
   const int32_t* unit_start;
   float* part_o;    // [R*2*G][64][512]
@@ -320,10 +353,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
       p.tok[t] = ti;
       if (units == 0) {
         // padding / uncovered token: zero output and LSE (golden.py leaves them zero)
-        uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * p.dtype_bytes);
-        for (int i = 0; i < p.H * D * p.dtype_bytes / 16; ++i) o[i] = make_uint4(0, 0, 0, 0);
-        if (p.lse)
-          for (int h = 0; h < p.H; ++h) p.lse[(size_t)t * p.H + h] = 0.f;
+        p.od.zero_token(t, p.H, 0, 1);
       }
     }
     // block exclusive scan of units
@@ -682,10 +712,9 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
     }
     const float L = m + __log2f(den);
     lse_s[c] = L;
-    if (p.lse) p.lse[(size_t)t * p.H + h] = L * kLn2;
+    p.od.lse_st(t, h, L * kLn2);
   }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 22)) return false;
-  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + ((size_t)t * p.H + g * HG) * D;
   constexpr int kHB = 8;
 #pragma unroll 1
   for (int h0 = G.hb; h0 < hend; h0 += kHB) {
@@ -719,7 +748,7 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
         uint2 o;
         o.x = IO::pack(acc[j].x, acc[j].y);
         o.y = IO::pack(acc[j].z, acc[j].w);
-        reinterpret_cast<uint2*>(outp + (size_t)(h0 + j) * D)[G.gst] = o;
+        p.od.st64(t, g * HG + h0 + j, 4 * G.gst, o);
       }
     }
   }
@@ -890,10 +919,9 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
     for (int i = 0; i < np; ++i) den += sas::ex2(li[i] - M);
     const float lse = M + __log2f(den);
     for (int i = 0; i < np; ++i) mw[i * 64 + c] = sas::ex2(li[i] - lse);
-    if (p.lse && h < p.H) p.lse[(size_t)t * p.H + h] = lse * kLn2;
+    if (h < p.H) p.od.lse_st(t, h, lse * kLn2);
   }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 23)) return false;
-  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)t * p.H * D;
   const int row = G.gst;
   const bool odd = G.lane & 1;
   const int d_even = row & ~1;
@@ -930,7 +958,7 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
       const float recv = __shfl_xor_sync(0xffffffffu, odd ? acc[h] : acc[h + 8], 1);
       const uint32_t w = odd ? IO::pack(recv, acc[h + 8]) : IO::pack(acc[h], recv);
       const int hh = g * HG + G.hb + hs + (odd ? h + 8 : h);
-      if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+      if (hh < p.H) p.od.st32(t, hh, j * 128 + d_even, w);
     }
   }
   return true;
@@ -969,7 +997,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
       const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
       const float Lf = L + sas::ex2(sink - m);
       S.inv[c] = 1.f / Lf;
-      if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+      if (h < p.H) p.od.lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
     } else {
       S.inv[c] = L > 0.f ? 1.f / L : 0.f;
     }
@@ -996,7 +1024,6 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
     // direct stores: lanes pair up (row, row^1); the even lane stores head h
     // for both rows, the odd lane head h+16 (4-byte stores; no shared-memory
     // staging, which would compete with the MMA operand reads)
-    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
     const bool odd = G.lane & 1;
     const int d_even = row & ~1;
 #pragma unroll 1
@@ -1011,7 +1038,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
         const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
         const int hh = g * HG + G.hb + (odd ? h + 16 : h);
-        if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+        if (hh < p.H) p.od.st32(sg.t, hh, j * 128 + d_even, w);
       }
     }
   } else {
@@ -1096,7 +1123,7 @@ __device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup&
     const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
     const float Lf = L + sas::ex2(sink - m);
     S.inv[c] = 1.f / Lf;
-    if (p.lse && h < p.H) p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+    if (h < p.H) p.od.lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
   }
   return true;
 }
@@ -1112,7 +1139,6 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
   // direct stores: lanes pair up (row, row^1); the even lane stores head h
   // for both rows, the odd lane head h+16
   const int row = G.gst;  // d within an O^T tile
-  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
   const bool odd = G.lane & 1;
   const int d_even = row & ~1;
 #pragma unroll 1
@@ -1127,7 +1153,7 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
       const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
       const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
       const int hh = g * HG + G.hb + (odd ? h + 16 : h);
-      if (hh < p.H) *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+      if (hh < p.H) p.od.st32(sg.t, hh, j * 128 + d_even, w);
     }
   }
   sas::tc_fence_before();
@@ -1169,13 +1195,12 @@ __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us
     int covered;
     if (!G.gs.sync_or(q >= lin0 && q < lin1, G.lane, G.lead, covered, abort_flag, p.status, 24)) return false;
     if (covered) continue;
-    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
     for (int h = 0; h < 32; ++h) {
       const int hh = g * HG + G.hb + h;
       if (hh < p.H)
-        for (int j = 0; j < 4; ++j) outp[(size_t)hh * D + j * 128 + G.gst] = IO::zero();
+        for (int j = 0; j < 4; ++j) p.od.st16(sg.t, hh, j * 128 + G.gst, 0);
     }
-    if (p.lse && G.gst < 32 && g * HG + G.hb + G.gst < p.H) p.lse[(size_t)sg.t * p.H + g * HG + G.hb + G.gst] = 0.f;
+    if (G.gst < 32 && g * HG + G.hb + G.gst < p.H) p.od.lse_st(sg.t, g * HG + G.hb + G.gst, 0.f);
   }
   return true;
 }
@@ -1242,10 +1267,7 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
   // tokens without work keep zero output and LSE (golden.py leaves them zero)
   for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
     if (s_us[t] != 0) continue;
-    uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * 2);
-    for (int i = tid; i < p.H * D * 2 / 16; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
-    if (p.lse)
-      for (int h = tid; h < p.H; h += kThreads) p.lse[(size_t)t * p.H + h] = 0.f;
+    p.od.zero_token(t, p.H, tid, kThreads);
   }
   // exclusive scan of the units, in place: each thread a run of <= 2 tokens
   constexpr int kPer = (kFusedMaxT + kThreads - 1) / kThreads;
@@ -1929,15 +1951,16 @@ extern "C" size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads,
   return ws_layout(num_tokens, num_heads, num_sms).total;
 }
 
-extern "C" int sas_sparse_attn_sharedkv_fwd(
-    const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype, int32_t layout_q,
-    int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q, const int32_t* seqused_kv, const void* ori_kv,
-    int64_t ori_num_blocks, int32_t ori_block_size, const int32_t* ori_block_table, int32_t ori_table_stride,
-    const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size, const int32_t* cmp_block_table,
-    int32_t cmp_table_stride, const int32_t* cmp_sparse_indices, int32_t topk, const float* sinks,
-    const int32_t* metadata, float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
-    void* out, float* lse, int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace,
-    size_t workspace_bytes, void* stream) {
+namespace {
+int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype, int32_t layout_q,
+             int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q, const int32_t* seqused_kv,
+             const void* ori_kv, int64_t ori_num_blocks, int32_t ori_block_size, const int32_t* ori_block_table,
+             int32_t ori_table_stride, const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size,
+             const int32_t* cmp_block_table, int32_t cmp_table_stride, const int32_t* cmp_sparse_indices,
+             int32_t topk, const float* sinks, const int32_t* metadata, float softmax_scale, int32_t cmp_ratio,
+             int32_t ori_win_left, int32_t scenario, const OutDesc& od, int32_t num_sms, int32_t stage_mask,
+             int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
+  void* out = od.out[0];
   if (head_dim != D) return SAS_ERR_UNSUPPORTED;
   if (num_heads <= 0 || num_heads % 8 != 0) return SAS_ERR_UNSUPPORTED;
   if (dtype != SAS_DTYPE_BF16 && dtype != SAS_DTYPE_FP16) return SAS_ERR_UNSUPPORTED;
@@ -1989,9 +2012,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   pp.tok = reinterpret_cast<TokInfo*>(ws + wl.tok);
   pp.unit_start = reinterpret_cast<int32_t*>(ws + wl.unit);
   pp.H = num_heads;
-  pp.dtype_bytes = 2;
-  pp.out = out;
-  pp.lse = lse;
+  pp.od = od;
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
 
@@ -2029,8 +2050,7 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
   fp.idx = cmp_sparse_indices;
   fp.sinks = sinks;
   fp.scale_log2 = softmax_scale * kLog2e;
-  fp.out = out;
-  fp.lse = lse;
+  fp.od = od;
   fp.tok = pp.tok;
   fp.unit_start = pp.unit_start;
   fp.part_o = reinterpret_cast<float*>(ws + wl.po);
@@ -2085,4 +2105,57 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
     if (e != cudaSuccess) return SAS_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? SAS_OK : SAS_ERR_CUDA;
+}
+}  // namespace
+
+extern "C" int sas_sparse_attn_sharedkv_fwd(
+    const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype, int32_t layout_q,
+    int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q, const int32_t* seqused_kv, const void* ori_kv,
+    int64_t ori_num_blocks, int32_t ori_block_size, const int32_t* ori_block_table, int32_t ori_table_stride,
+    const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size, const int32_t* cmp_block_table,
+    int32_t cmp_table_stride, const int32_t* cmp_sparse_indices, int32_t topk, const float* sinks,
+    const int32_t* metadata, float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
+    void* out, float* lse, int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace,
+    size_t workspace_bytes, void* stream) {
+  OutDesc od{};
+  od.out[0] = static_cast<uint8_t*>(out);
+  od.lse[0] = lse;
+  od.n = 1;
+  od.H_total = num_heads;
+  od.h0 = 0;
+  return fwd_impl(q, num_tokens, num_heads, head_dim, dtype, layout_q, batch, max_seqlen_q, cu_seqlens_q, seqused_kv,
+                  ori_kv, ori_num_blocks, ori_block_size, ori_block_table, ori_table_stride, cmp_kv, cmp_num_blocks,
+                  cmp_block_size, cmp_block_table, cmp_table_stride, cmp_sparse_indices, topk, sinks, metadata,
+                  softmax_scale, cmp_ratio, ori_win_left, scenario, od, num_sms, stage_mask, status, workspace,
+                  workspace_bytes, stream);
+}
+
+extern "C" int sas_sparse_attn_sharedkv_fwd_gather(
+    const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype, int32_t layout_q,
+    int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q, const int32_t* seqused_kv, const void* ori_kv,
+    int64_t ori_num_blocks, int32_t ori_block_size, const int32_t* ori_block_table, int32_t ori_table_stride,
+    const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size, const int32_t* cmp_block_table,
+    int32_t cmp_table_stride, const int32_t* cmp_sparse_indices, int32_t topk, const float* sinks,
+    const int32_t* metadata, float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
+    void* const* outs, float* const* lses, int32_t n_out, int32_t out_heads_total, int32_t out_head_offset,
+    int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!outs || n_out < 1 || n_out > kMaxOut || out_head_offset < 0 || out_heads_total < out_head_offset + num_heads)
+    return SAS_ERR_INVALID_ARG;
+  if (stage_mask & SAS_FLAG_AFTER_METADATA) return SAS_ERR_INVALID_ARG;
+  if (g_cut_cost >= 0) return SAS_ERR_UNSUPPORTED;  // split tokens merge through one output
+  OutDesc od{};
+  for (int k = 0; k < n_out; ++k) {
+    if (!outs[k]) return SAS_ERR_INVALID_ARG;
+    od.out[k] = static_cast<uint8_t*>(outs[k]);
+    od.lse[k] = lses ? lses[k] : nullptr;
+    if (lses && !lses[k]) return SAS_ERR_INVALID_ARG;
+  }
+  od.n = n_out;
+  od.H_total = out_heads_total;
+  od.h0 = out_head_offset;
+  return fwd_impl(q, num_tokens, num_heads, head_dim, dtype, layout_q, batch, max_seqlen_q, cu_seqlens_q, seqused_kv,
+                  ori_kv, ori_num_blocks, ori_block_size, ori_block_table, ori_table_stride, cmp_kv, cmp_num_blocks,
+                  cmp_block_size, cmp_block_table, cmp_table_stride, cmp_sparse_indices, topk, sinks, metadata,
+                  softmax_scale, cmp_ratio, ori_win_left, scenario, od, num_sms, stage_mask, status, workspace,
+                  workspace_bytes, stream);
 }

@@ -8,9 +8,14 @@ The op has no exchange step between requests, so it shards two ways:
   requests (longest first, capped at ceil(B / world) per rank) and
   ``select_requests`` cuts a rank's batch out of a full one.
 * head-sharded: every rank computes ``H / world`` query heads of every
-  request and the outputs are all-gathered (NCCL over NVLink on GPUs). The
-  KV rows are shared by all heads, so each rank still reads every KV row:
-  this mode trades bandwidth for latency by construction.
+  request and every rank ends with all heads. ``head_sharded_forward_p2p``
+  (GPUs, NCCL group) has the attention kernel itself store each result into
+  every rank's output buffer through peer pointers into symmetric memory
+  (NVLink), so the gather happens while the kernel computes;
+  ``head_sharded_forward`` runs the kernel and then an NCCL all-gather (also
+  the form the gloo CPU tests use). The KV rows are shared by all heads, so
+  each rank still reads every KV row: this mode trades bandwidth for latency
+  by construction.
 """
 
 from __future__ import annotations
@@ -110,4 +115,51 @@ def head_sharded_forward(q: torch.Tensor, *, group: Optional[dist.ProcessGroup] 
     _all_gather(l_all, l_loc.contiguous(), group)
     out = o_all.permute(1, 0, 2, 3).reshape(T, H, D)
     lse = l_all.permute(1, 0, 2).reshape(T, H)
+    return out, lse
+
+
+_SYMM: Dict[tuple, tuple] = {}
+
+
+def _symmetric_outputs(T: int, H: int, dtype, device, group):
+    """Cached symmetric-memory output and LSE buffers of this rank, with the
+    device pointers of every rank's copies."""
+    import os
+
+    # plain peer pointers are all the kernel uses: no NVLink multicast object
+    os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+    import torch.distributed._symmetric_memory as symm_mem
+
+    key = (T, H, dtype, device.index, id(group))
+    if key not in _SYMM:
+        out = symm_mem.empty((T, H, 512), dtype=dtype, device=device)
+        lse = symm_mem.empty((T, H), dtype=torch.float32, device=device)
+        gname = group.group_name if group is not None else dist.group.WORLD.group_name
+        ho = symm_mem.rendezvous(out, gname)
+        hl = symm_mem.rendezvous(lse, gname)
+        _SYMM[key] = (out, lse, ho, hl, list(ho.buffer_ptrs), list(hl.buffer_ptrs))
+    return _SYMM[key]
+
+
+def head_sharded_forward_p2p(q: torch.Tensor, *, group: Optional[dist.ProcessGroup] = None, **kw):
+    """Head-sharded forward whose gather is done by the attention kernel's own
+    peer stores (``sas_sparse_attn_sharedkv_fwd_gather``): this rank computes
+    heads ``[rank * H / world, (rank + 1) * H / world)`` and writes them into
+    the symmetric output buffers of all ranks. Returns this rank's buffers
+    ``(out [T, H, 512], lse [T, H])``, complete once every rank has written;
+    they are reused by the next call with the same shape."""
+    from .api import sparse_attn_sharedkv
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    T, H, D = q.shape
+    h0, h1 = head_range(H, world, rank)
+    out, lse, ho, hl, optrs, lptrs = _symmetric_outputs(T, H, q.dtype, q.device, group)
+    sinks = kw.pop("sinks")
+    kw.pop("out", None)
+    kw.pop("lse_out", None)
+    ho.barrier(channel=0)  # every rank is done reading the buffers' previous contents
+    sparse_attn_sharedkv(q[:, h0:h1].contiguous(), sinks=sinks[h0:h1].contiguous(),
+                         _gather=(optrs, lptrs, H, h0), **kw)
+    ho.barrier(channel=1)  # every rank's stores into this rank's buffers are done
     return out, lse

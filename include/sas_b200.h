@@ -183,6 +183,33 @@ int sas_sparse_attn_sharedkv_fwd(
     int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes,
     void* stream);
 
+/* Head-sharded forward for one rank of n (no counterpart in the reference,
+ * whose op runs on one device): the call computes heads [out_head_offset,
+ * out_head_offset + num_heads) of q (passed as this rank's slice) and writes
+ * every output and LSE value straight into all n buffers outs[k] / lses[k],
+ * each [num_tokens, out_heads_total, 512] / [num_tokens, out_heads_total] -
+ * the rank's own and its peers', as device pointers into peer-accessible
+ * (symmetric) memory over NVLink. The all-gather of the head-sharded mode is
+ * thereby done by the attention kernel's own stores, overlapped with its
+ * compute; the caller fences the ranks before and after the call (a buffer
+ * must not be read by its owner while peers write it). n <= 8, lses may be
+ * NULL, SAS_FLAG_AFTER_METADATA and SAS_OPT_SPLIT_TOKENS are not accepted.
+ * Other arguments as sas_sparse_attn_sharedkv_fwd. */
+int sas_sparse_attn_sharedkv_fwd_gather(
+    const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype,
+    int32_t layout_q, int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q,
+    const int32_t* seqused_kv,
+    const void* ori_kv, int64_t ori_num_blocks, int32_t ori_block_size,
+    const int32_t* ori_block_table, int32_t ori_table_stride,
+    const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size,
+    const int32_t* cmp_block_table, int32_t cmp_table_stride,
+    const int32_t* cmp_sparse_indices, int32_t topk,
+    const float* sinks, const int32_t* metadata,
+    float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
+    void* const* outs, float* const* lses, int32_t n_out, int32_t out_heads_total, int32_t out_head_offset,
+    int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes,
+    void* stream);
+
 /* ------------------------------------------------------------------------
  * Backward, consuming the forward's LSE. The reference documents the LSE as
  * the input of a FlashAttention-2 style backward

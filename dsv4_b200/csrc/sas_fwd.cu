@@ -164,11 +164,11 @@ struct TokInfo {
   int b, s_g, n_cmp, thr;
 };
 
-// Where a call's results go. Normally one output [T, H, 512] and one LSE
-// [T, H]. The head-sharded multi-GPU forward computes heads [h0, h0 + H) of
-// outputs that hold H_total heads per token, and writes every result into
-// the output buffers of all n ranks (peer pointers into symmetric memory), so
-// the outputs are gathered as they are produced and no all-gather follows.
+// Outputs of the head-sharded multi-GPU forward (the GA kernel variants): the
+// call computes heads [h0, h0 + H) of outputs holding H_total heads per
+// token and writes every result into the output buffers of all n ranks
+// (peer pointers into symmetric memory), so the outputs are gathered as they
+// are produced and no all-gather follows. Lives in the workspace.
 constexpr int kMaxOut = 8;
 struct OutDesc {
   uint8_t* out[kMaxOut];
@@ -176,13 +176,16 @@ struct OutDesc {
   int n, H_total, h0;
   __device__ __forceinline__ size_t row(int t, int hh) const { return (size_t)t * H_total + h0 + hh; }
   __device__ __forceinline__ void st32(int t, int hh, int col, uint32_t w) const {
-    for (int k = 0; k < n; ++k) *reinterpret_cast<uint32_t*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+    const size_t off = (row(t, hh) * D + col) * 2;
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint32_t*>(out[k] + off) = w;
   }
   __device__ __forceinline__ void st64(int t, int hh, int col, uint2 w) const {
-    for (int k = 0; k < n; ++k) *reinterpret_cast<uint2*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+    const size_t off = (row(t, hh) * D + col) * 2;
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint2*>(out[k] + off) = w;
   }
   __device__ __forceinline__ void st16(int t, int hh, int col, uint16_t w) const {
-    for (int k = 0; k < n; ++k) *reinterpret_cast<uint16_t*>(out[k] + (row(t, hh) * D + col) * 2) = w;
+    const size_t off = (row(t, hh) * D + col) * 2;
+    for (int k = 0; k < n; ++k) *reinterpret_cast<uint16_t*>(out[k] + off) = w;
   }
   __device__ __forceinline__ void lse_st(int t, int hh, float v) const {
     if (lse[0])
@@ -206,10 +209,12 @@ struct PlanParams {
   const int32_t* meta;
   TokInfo* tok;
   int32_t* unit_start;  // [T+1]
-  int H;
-  OutDesc od;           // rows of tokens without work are zeroed here
+  int H, dtype_bytes;
+  void* out;            // rows of tokens without work are zeroed here
+  float* lse;
   int32_t* merge_cnt;   // [n_cnt] split-token arrival counters, zeroed here
   int n_cnt;
+  const OutDesc* god;   // head-sharded outputs (nullptr: out / lse above)
 };
 
 struct FwdParams {
@@ -223,7 +228,8 @@ struct FwdParams {
   const int32_t* idx;
   const float* sinks;
   float scale_log2;
-  OutDesc od;
+  void* out;
+  float* lse;
   const TokInfo* tok;
   const int32_t* unit_start;
   float* part_o;    // [R*2*G][64][512]
@@ -242,6 +248,7 @@ struct FwdParams {
   const int32_t* seqused_kv;
   const int32_t* meta;
   unsigned long long* trace; // optional per-CTA cycle counters (nullptr in production)
+  const OutDesc* god;        // head-sharded outputs, read by the GA kernel variants only
 };
 
 // trace slots per CTA (SM cycles, accumulated by one thread of each role)
@@ -353,7 +360,14 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
       p.tok[t] = ti;
       if (units == 0) {
         // padding / uncovered token: zero output and LSE (golden.py leaves them zero)
-        p.od.zero_token(t, p.H, 0, 1);
+        if (p.god) {
+          p.god->zero_token(t, p.H, 0, 1);
+        } else {
+          uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * p.dtype_bytes);
+          for (int i = 0; i < p.H * D * p.dtype_bytes / 16; ++i) o[i] = make_uint4(0, 0, 0, 0);
+          if (p.lse)
+            for (int h = 0; h < p.H; ++h) p.lse[(size_t)t * p.H + h] = 0.f;
+        }
       }
     }
     // block exclusive scan of units
@@ -694,7 +708,7 @@ __device__ __forceinline__ size_t part_slot(const FwdParams& p, int rr, int r0, 
   return ((size_t)rr * 2 + (rr == r0 ? wf : 0)) * p.G + g;
 }
 
-template <int DT>
+template <int DT, bool GA>
 __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g, int r0, int r1, int wf,
                                                 SmGroup& G, float* lse_s, volatile sas::CtaCtl* abort_flag) {
   using IO = IoType<DT>;
@@ -712,9 +726,11 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
     }
     const float L = m + __log2f(den);
     lse_s[c] = L;
-    p.od.lse_st(t, h, L * kLn2);
+    if constexpr (GA) p.god->lse_st(t, h, L * kLn2);
+    else if (p.lse) p.lse[(size_t)t * p.H + h] = L * kLn2;
   }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 22)) return false;
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + ((size_t)t * p.H + g * HG) * D;
   constexpr int kHB = 8;
 #pragma unroll 1
   for (int h0 = G.hb; h0 < hend; h0 += kHB) {
@@ -748,7 +764,8 @@ __device__ __forceinline__ bool merge_cut_token(const FwdParams& p, int t, int g
         uint2 o;
         o.x = IO::pack(acc[j].x, acc[j].y);
         o.y = IO::pack(acc[j].z, acc[j].w);
-        p.od.st64(t, g * HG + h0 + j, 4 * G.gst, o);
+        if constexpr (GA) p.god->st64(t, g * HG + h0 + j, 4 * G.gst, o);
+        else reinterpret_cast<uint2*>(outp + (size_t)(h0 + j) * D)[G.gst] = o;
       }
     }
   }
@@ -897,7 +914,7 @@ __device__ __forceinline__ bool chunk_exp_pass(const FwdParams& p, SmGroup& G, c
 // bit-identical to the partial it would have written. Every piece enters the
 // same way in range order, so the result does not depend on which piece
 // merges: lse = log2(2^sink + sum_i 2^lse_i), out = sum_i 2^(lse_i - lse) o_i.
-template <int DT>
+template <int DT, bool GA>
 __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, const SmShared& S, float* mw,
                                                 int t, int g, int r0, int r1, int wf, int own_r,
                                                 volatile sas::CtaCtl* abort_flag) {
@@ -919,9 +936,14 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
     for (int i = 0; i < np; ++i) den += sas::ex2(li[i] - M);
     const float lse = M + __log2f(den);
     for (int i = 0; i < np; ++i) mw[i * 64 + c] = sas::ex2(li[i] - lse);
-    if (h < p.H) p.od.lse_st(t, h, lse * kLn2);
+    if constexpr (GA) {
+      if (h < p.H) p.god->lse_st(t, h, lse * kLn2);
+    } else if (p.lse && h < p.H) {
+      p.lse[(size_t)t * p.H + h] = lse * kLn2;
+    }
   }
   if (!G.gs.sync(G.lane, G.lead, abort_flag, p.status, 23)) return false;
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)t * p.H * D;
   const int row = G.gst;
   const bool odd = G.lane & 1;
   const int d_even = row & ~1;
@@ -958,7 +980,11 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
       const float recv = __shfl_xor_sync(0xffffffffu, odd ? acc[h] : acc[h + 8], 1);
       const uint32_t w = odd ? IO::pack(recv, acc[h + 8]) : IO::pack(acc[h], recv);
       const int hh = g * HG + G.hb + hs + (odd ? h + 8 : h);
-      if (hh < p.H) p.od.st32(t, hh, j * 128 + d_even, w);
+      if constexpr (GA) {
+        if (hh < p.H) p.god->st32(t, hh, j * 128 + d_even, w);
+      } else if (hh < p.H) {
+        *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+      }
     }
   }
   return true;
@@ -970,7 +996,7 @@ __device__ __forceinline__ bool merge_from_tmem(const FwdParams& p, SmGroup& G, 
 // leaves a normalised partial (o, lse2); the last merges them. If all other
 // pieces are already in when a CTA gets here, it merges from its own TMEM and
 // never writes its partial.
-template <int DT>
+template <int DT, bool GA>
 __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G, const SmShared& S, uint64_t* bars,
                                                  const Seg& sg, int r, int g, volatile sas::CtaCtl* abort_flag, bool tracing,
                                                  unsigned long long* tr) {
@@ -997,7 +1023,11 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
       const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
       const float Lf = L + sas::ex2(sink - m);
       S.inv[c] = 1.f / Lf;
-      if (h < p.H) p.od.lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
+      if constexpr (GA) {
+        if (h < p.H) p.god->lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
+      } else if (p.lse && h < p.H) {
+        p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+      }
     } else {
       S.inv[c] = L > 0.f ? 1.f / L : 0.f;
     }
@@ -1024,6 +1054,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
     // direct stores: lanes pair up (row, row^1); the even lane stores head h
     // for both rows, the odd lane head h+16 (4-byte stores; no shared-memory
     // staging, which would compete with the MMA operand reads)
+    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
     const bool odd = G.lane & 1;
     const int d_even = row & ~1;
 #pragma unroll 1
@@ -1038,7 +1069,11 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
         const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
         const int hh = g * HG + G.hb + (odd ? h + 16 : h);
-        if (hh < p.H) p.od.st32(sg.t, hh, j * 128 + d_even, w);
+        if constexpr (GA) {
+          if (hh < p.H) p.god->st32(sg.t, hh, j * 128 + d_even, w);
+        } else if (hh < p.H) {
+          *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+        }
       }
     }
   } else {
@@ -1077,14 +1112,14 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
         tmem_merge = 1;
       } else {
         __threadfence();
-        if (!merge_cut_token<DT>(p, sg.t, g, r0, r1, wf, G, S.scratch, abort_flag)) return false;
+        if (!merge_cut_token<DT, GA>(p, sg.t, g, r0, r1, wf, G, S.scratch, abort_flag)) return false;
       }
     }
     }
     if (tmem_merge) {
       __threadfence();
       float* mw = S.scratch;
-      if (!merge_from_tmem<DT>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
+      if (!merge_from_tmem<DT, GA>(p, G, S, mw, sg.t, g, r0, r1, wf, r, abort_flag)) return false;
     }
   }
   sas::tc_fence_before();
@@ -1107,7 +1142,7 @@ __device__ __forceinline__ bool segment_epilogue(const FwdParams& p, SmGroup& G,
 //    released to the MMA.
 // The next tile's max pass holds a group barrier, which orders the first
 // half's shared-memory writes before the second half's reads.
-template <int DT>
+template <int DT, bool GA>
 __device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup& G, const SmShared& S, const Seg& sg,
                                                     int g, volatile sas::CtaCtl* abort_flag) {
   float l[32];
@@ -1123,12 +1158,16 @@ __device__ __forceinline__ bool epilogue_first_half(const FwdParams& p, SmGroup&
     const float sink = h < p.H ? p.sinks[h] * kLog2e : 0.f;
     const float Lf = L + sas::ex2(sink - m);
     S.inv[c] = 1.f / Lf;
-    if (h < p.H) p.od.lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
+    if constexpr (GA) {
+      if (h < p.H) p.god->lse_st(sg.t, h, (m + __log2f(Lf)) * kLn2);
+    } else if (p.lse && h < p.H) {
+      p.lse[(size_t)sg.t * p.H + h] = (m + __log2f(Lf)) * kLn2;
+    }
   }
   return true;
 }
 
-template <int DT>
+template <int DT, bool GA>
 __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup& G, const SmShared& S,
                                                      uint64_t* bars, const Seg& sg, int g, volatile sas::CtaCtl* abort_flag,
                                                      bool tracing, unsigned long long* tr) {
@@ -1139,6 +1178,7 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
   // direct stores: lanes pair up (row, row^1); the even lane stores head h
   // for both rows, the odd lane head h+16
   const int row = G.gst;  // d within an O^T tile
+  typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
   const bool odd = G.lane & 1;
   const int d_even = row & ~1;
 #pragma unroll 1
@@ -1153,7 +1193,11 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
       const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
       const uint32_t w = odd ? IO::pack(recv, v1) : IO::pack(v0, recv);
       const int hh = g * HG + G.hb + (odd ? h + 16 : h);
-      if (hh < p.H) p.od.st32(sg.t, hh, j * 128 + d_even, w);
+      if constexpr (GA) {
+        if (hh < p.H) p.god->st32(sg.t, hh, j * 128 + d_even, w);
+      } else if (hh < p.H) {
+        *reinterpret_cast<uint32_t*>(outp + (size_t)hh * D + j * 128 + d_even) = w;
+      }
     }
   }
   sas::tc_fence_before();
@@ -1172,7 +1216,7 @@ __device__ __forceinline__ bool epilogue_second_half(const FwdParams& p, SmGroup
 // its heads of every token that no core window covers (the reference leaves
 // those zero). The piece that merges a cut token does this after its merge,
 // so an uncovered cut token ends zero whatever the order of the pieces.
-template <int DT>
+template <int DT, bool GA>
 __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us, const TokInfo* tok,
                                const int* s_smax, const RangeInfo& ri, int g, volatile sas::CtaCtl* abort_flag) {
   using IO = IoType<DT>;
@@ -1195,12 +1239,20 @@ __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us
     int covered;
     if (!G.gs.sync_or(q >= lin0 && q < lin1, G.lane, G.lead, covered, abort_flag, p.status, 24)) return false;
     if (covered) continue;
+    typename IO::T* outp = reinterpret_cast<typename IO::T*>(p.out) + (size_t)sg.t * p.H * D;
     for (int h = 0; h < 32; ++h) {
       const int hh = g * HG + G.hb + h;
       if (hh < p.H)
-        for (int j = 0; j < 4; ++j) p.od.st16(sg.t, hh, j * 128 + G.gst, 0);
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (GA) p.god->st16(sg.t, hh, j * 128 + G.gst, 0);
+          else outp[(size_t)hh * D + j * 128 + G.gst] = IO::zero();
+        }
     }
-    if (G.gst < 32 && g * HG + G.hb + G.gst < p.H) p.od.lse_st(sg.t, g * HG + G.hb + G.gst, 0.f);
+    if constexpr (GA) {
+      if (G.gst < 32 && g * HG + G.hb + G.gst < p.H) p.god->lse_st(sg.t, g * HG + G.hb + G.gst, 0.f);
+    } else if (p.lse && G.gst < 32 && g * HG + G.hb + G.gst < p.H) {
+      p.lse[(size_t)sg.t * p.H + g * HG + G.hb + G.gst] = 0.f;
+    }
   }
   return true;
 }
@@ -1211,7 +1263,7 @@ __device__ bool zero_uncovered(const FwdParams& p, SmGroup& G, const int32_t* us
 // epilogue checks it before writing a token), so none of this reads the
 // metadata and it can run while the metadata kernel is still in flight.
 // Output rows of tokens without work are zeroed, each by one CTA.
-template <int DT>
+template <int DT, bool GA>
 __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, int* s_smax, int* s_wsum) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int kW = kThreads / 32;
@@ -1267,7 +1319,14 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
   // tokens without work keep zero output and LSE (golden.py leaves them zero)
   for (int t = blockIdx.x; t < p.T; t += gridDim.x) {
     if (s_us[t] != 0) continue;
-    p.od.zero_token(t, p.H, tid, kThreads);
+    if constexpr (GA) {
+      p.god->zero_token(t, p.H, tid, kThreads);
+    } else {
+      uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + (size_t)t * p.H * D * 2);
+      for (int i = tid; i < p.H * D * 2 / 16; i += kThreads) o[i] = make_uint4(0, 0, 0, 0);
+      if (p.lse)
+        for (int h = tid; h < p.H; h += kThreads) p.lse[(size_t)t * p.H + h] = 0.f;
+    }
   }
   // exclusive scan of the units, in place: each thread a run of <= 2 tokens
   constexpr int kPer = (kFusedMaxT + kThreads - 1) / kThreads;
@@ -1301,7 +1360,7 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
 
 // TRACE = true builds the diagnostics variant that accumulates per-role cycle
 // counters into p.trace; the production variant carries none of that state.
-template <int DT, bool TRACE, bool FUSED>
+template <int DT, bool TRACE, bool FUSED, bool GA>
 __global__ void __launch_bounds__(kThreads, 1)
     sas_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const FwdParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1373,7 +1432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the metadata is only waited for when a token's output is written
   if (!p.early) sas::pdl_wait();
   if constexpr (FUSED)
-    fused_plan<DT>(p, s_tok, s_us,
+    fused_plan<DT, GA>(p, s_tok, s_us,
                    reinterpret_cast<int*>(smem + OFF_PLAN + P_SMAX), reinterpret_cast<int*>(red));
   if (warp == 0) {
     const RangeInfo ri = compute_range(usp, p.T, p.R, r, lane, p.cut_cost);
@@ -1759,26 +1818,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + (tl.g0 + i) % CD]);
         if (ok && i == 0 && pending) {
-          ok = epilogue_second_half<DT>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
+          ok = epilogue_second_half<DT, GA>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
           pending = false;
         }
       }
       ++gtile;
       if (ok && tl.last) {
         if (it.sg.complete) {
-          ok = epilogue_first_half<DT>(p, G, sm, it.sg, g, abort_flag);
+          ok = epilogue_first_half<DT, GA>(p, G, sm, it.sg, g, abort_flag);
           pend = it.sg;
           pending = true;
         } else {
-          ok = segment_epilogue<DT>(p, G, sm, bars, it.sg, r, g, abort_flag, trace_me, trp);
+          ok = segment_epilogue<DT, GA>(p, G, sm, bars, it.sg, r, g, abort_flag, trace_me, trp);
         }
       }
     }
     if (TRACE && tid == kSoftmaxWarp0 * 32) ev(13);
-    if (ok && pending) ok = epilogue_second_half<DT>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
+    if (ok && pending) ok = epilogue_second_half<DT, GA>(p, G, sm, bars, pend, g, abort_flag, trace_me, trp);
     if (TRACE && tid == kSoftmaxWarp0 * 32) ev(14);
     if (FUSED && ok)
-      zero_uncovered<DT>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
+      zero_uncovered<DT, GA>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
   }
 
@@ -1885,7 +1944,7 @@ int g_trace_dev = -1;      // the device that owns it
 unsigned long long g_wait_ns = SAS_WAIT_LIMIT_NS;
 
 struct WsLayout {
-  size_t tok, unit, po, pl, cnt, total;
+  size_t tok, unit, po, pl, cnt, od, total;
 };
 WsLayout ws_layout(int T, int H, int num_sms) {
   const int G = (H + HG - 1) / HG;
@@ -1896,7 +1955,8 @@ WsLayout ws_layout(int T, int H, int num_sms) {
   w.po = align_up(w.unit + sizeof(int32_t) * ((size_t)T + 1), 256);
   w.pl = align_up(w.po + sizeof(float) * (size_t)R * 2 * G * HG * D, 256);
   w.cnt = align_up(w.pl + sizeof(float) * (size_t)R * 2 * G * HG, 256);
-  w.total = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
+  w.od = align_up(w.cnt + sizeof(int32_t) * (size_t)R * G * 2, 256);
+  w.total = align_up(w.od + sizeof(OutDesc), 256);
   return w;
 }
 
@@ -1952,15 +2012,15 @@ extern "C" size_t sas_fwd_workspace_bytes(int32_t num_tokens, int32_t num_heads,
 }
 
 namespace {
+// The forward; host_od != nullptr selects the head-sharded outputs (GA kernels).
 int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_dim, int32_t dtype, int32_t layout_q,
              int32_t batch, int32_t max_seqlen_q, const int32_t* cu_seqlens_q, const int32_t* seqused_kv,
              const void* ori_kv, int64_t ori_num_blocks, int32_t ori_block_size, const int32_t* ori_block_table,
              int32_t ori_table_stride, const void* cmp_kv, int64_t cmp_num_blocks, int32_t cmp_block_size,
              const int32_t* cmp_block_table, int32_t cmp_table_stride, const int32_t* cmp_sparse_indices,
              int32_t topk, const float* sinks, const int32_t* metadata, float softmax_scale, int32_t cmp_ratio,
-             int32_t ori_win_left, int32_t scenario, const OutDesc& od, int32_t num_sms, int32_t stage_mask,
-             int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
-  void* out = od.out[0];
+             int32_t ori_win_left, int32_t scenario, void* out, float* lse, const OutDesc* host_od, int32_t num_sms,
+             int32_t stage_mask, int32_t* status, void* workspace, size_t workspace_bytes, void* stream) {
   if (head_dim != D) return SAS_ERR_UNSUPPORTED;
   if (num_heads <= 0 || num_heads % 8 != 0) return SAS_ERR_UNSUPPORTED;
   if (dtype != SAS_DTYPE_BF16 && dtype != SAS_DTYPE_FP16) return SAS_ERR_UNSUPPORTED;
@@ -2012,10 +2072,20 @@ int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_
   pp.tok = reinterpret_cast<TokInfo*>(ws + wl.tok);
   pp.unit_start = reinterpret_cast<int32_t*>(ws + wl.unit);
   pp.H = num_heads;
-  pp.od = od;
+  pp.dtype_bytes = 2;
+  pp.out = out;
+  pp.lse = lse;
   pp.merge_cnt = reinterpret_cast<int32_t*>(ws + wl.cnt);
   pp.n_cnt = R * G * 2;
 
+  const OutDesc* god = nullptr;
+  if (host_od) {
+    // the output descriptor goes to the workspace, where the GA kernels read it
+    god = reinterpret_cast<const OutDesc*>(ws + wl.od);
+    if (cudaMemcpyAsync(ws + wl.od, host_od, sizeof(OutDesc), cudaMemcpyHostToDevice, st) != cudaSuccess)
+      return SAS_ERR_CUDA;
+  }
+  pp.god = god;
   if ((stage_mask & SAS_STAGE_PLAN) && !fused) {
     if (launch_pdl(sas_plan_kernel, dim3(1), dim3(1024), 0, st, pp) != cudaSuccess) return SAS_ERR_CUDA;
   }
@@ -2050,7 +2120,8 @@ int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_
   fp.idx = cmp_sparse_indices;
   fp.sinks = sinks;
   fp.scale_log2 = softmax_scale * kLog2e;
-  fp.od = od;
+  fp.out = out;
+  fp.lse = lse;
   fp.tok = pp.tok;
   fp.unit_start = pp.unit_start;
   fp.part_o = reinterpret_cast<float*>(ws + wl.po);
@@ -2071,20 +2142,31 @@ int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_
   fp.seqused_kv = seqused_kv;
   fp.meta = metadata;
   fp.trace = g_trace;
+  fp.god = god;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return SAS_ERR_CUDA;
   static uint64_t attr_done = 0;  // bit per device
   if (!(attr_done & (1ull << dev))) {
     const int a = cudaFuncAttributeMaxDynamicSharedMemorySize;
-    if (cudaFuncSetAttribute(sas_fwd_kernel<0, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<0, true, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, true, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<0, false, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, false, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<0, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
-        cudaFuncSetAttribute(sas_fwd_kernel<1, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(sas_fwd_kernel<0, false, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, true, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, true, false, false>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, false, true, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, true, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, true, true, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, true, true, false>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, false, false, true>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, false, true>, (cudaFuncAttribute)a, SMEM_BYTES_BASE) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<0, false, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(sas_fwd_kernel<1, false, true, true>, (cudaFuncAttribute)a, SMEM_BYTES) != cudaSuccess)
       return SAS_ERR_CUDA;
     attr_done |= 1ull << dev;
   }
@@ -2094,13 +2176,17 @@ int fwd_impl(const void* q, int32_t num_tokens, int32_t num_heads, int32_t head_
     const bool tr = fp.trace != nullptr;
     const dim3 grid(R * G), block(kThreads);
     using KernelFn = void (*)(const CUtensorMap, const FwdParams);
-    // [dtype][trace][fused]
+    // [dtype][trace][fused]; head-sharded outputs: [dtype][fused] (no trace)
     static const KernelFn kernels[2][2][2] = {
-        {{sas_fwd_kernel<0, false, false>, sas_fwd_kernel<0, false, true>},
-         {sas_fwd_kernel<0, true, false>, sas_fwd_kernel<0, true, true>}},
-        {{sas_fwd_kernel<1, false, false>, sas_fwd_kernel<1, false, true>},
-         {sas_fwd_kernel<1, true, false>, sas_fwd_kernel<1, true, true>}}};
-    const KernelFn k = kernels[dtype == SAS_DTYPE_BF16 ? 0 : 1][tr ? 1 : 0][fused ? 1 : 0];
+        {{sas_fwd_kernel<0, false, false, false>, sas_fwd_kernel<0, false, true, false>},
+         {sas_fwd_kernel<0, true, false, false>, sas_fwd_kernel<0, true, true, false>}},
+        {{sas_fwd_kernel<1, false, false, false>, sas_fwd_kernel<1, false, true, false>},
+         {sas_fwd_kernel<1, true, false, false>, sas_fwd_kernel<1, true, true, false>}}};
+    static const KernelFn ga_kernels[2][2] = {
+        {sas_fwd_kernel<0, false, false, true>, sas_fwd_kernel<0, false, true, true>},
+        {sas_fwd_kernel<1, false, false, true>, sas_fwd_kernel<1, false, true, true>}};
+    const int di = dtype == SAS_DTYPE_BF16 ? 0 : 1;
+    const KernelFn k = god ? ga_kernels[di][fused ? 1 : 0] : kernels[di][tr ? 1 : 0][fused ? 1 : 0];
     const cudaError_t e = launch_pdl(k, grid, block, fused ? SMEM_BYTES : SMEM_BYTES_BASE, st, tm_q, fp);
     if (e != cudaSuccess) return SAS_ERR_CUDA;
   }
@@ -2117,17 +2203,11 @@ extern "C" int sas_sparse_attn_sharedkv_fwd(
     const int32_t* metadata, float softmax_scale, int32_t cmp_ratio, int32_t ori_win_left, int32_t scenario,
     void* out, float* lse, int32_t num_sms, int32_t stage_mask, int32_t* status, void* workspace,
     size_t workspace_bytes, void* stream) {
-  OutDesc od{};
-  od.out[0] = static_cast<uint8_t*>(out);
-  od.lse[0] = lse;
-  od.n = 1;
-  od.H_total = num_heads;
-  od.h0 = 0;
   return fwd_impl(q, num_tokens, num_heads, head_dim, dtype, layout_q, batch, max_seqlen_q, cu_seqlens_q, seqused_kv,
                   ori_kv, ori_num_blocks, ori_block_size, ori_block_table, ori_table_stride, cmp_kv, cmp_num_blocks,
                   cmp_block_size, cmp_block_table, cmp_table_stride, cmp_sparse_indices, topk, sinks, metadata,
-                  softmax_scale, cmp_ratio, ori_win_left, scenario, od, num_sms, stage_mask, status, workspace,
-                  workspace_bytes, stream);
+                  softmax_scale, cmp_ratio, ori_win_left, scenario, out, lse, nullptr, num_sms, stage_mask, status,
+                  workspace, workspace_bytes, stream);
 }
 
 extern "C" int sas_sparse_attn_sharedkv_fwd_gather(
@@ -2142,13 +2222,12 @@ extern "C" int sas_sparse_attn_sharedkv_fwd_gather(
   if (!outs || n_out < 1 || n_out > kMaxOut || out_head_offset < 0 || out_heads_total < out_head_offset + num_heads)
     return SAS_ERR_INVALID_ARG;
   if (stage_mask & SAS_FLAG_AFTER_METADATA) return SAS_ERR_INVALID_ARG;
-  if (g_cut_cost >= 0) return SAS_ERR_UNSUPPORTED;  // split tokens merge through one output
+  if (g_cut_cost >= 0 || g_trace) return SAS_ERR_UNSUPPORTED;  // split tokens merge through one output
   OutDesc od{};
   for (int k = 0; k < n_out; ++k) {
-    if (!outs[k]) return SAS_ERR_INVALID_ARG;
+    if (!outs[k] || (lses && !lses[k])) return SAS_ERR_INVALID_ARG;
     od.out[k] = static_cast<uint8_t*>(outs[k]);
     od.lse[k] = lses ? lses[k] : nullptr;
-    if (lses && !lses[k]) return SAS_ERR_INVALID_ARG;
   }
   od.n = n_out;
   od.H_total = out_heads_total;
@@ -2156,6 +2235,6 @@ extern "C" int sas_sparse_attn_sharedkv_fwd_gather(
   return fwd_impl(q, num_tokens, num_heads, head_dim, dtype, layout_q, batch, max_seqlen_q, cu_seqlens_q, seqused_kv,
                   ori_kv, ori_num_blocks, ori_block_size, ori_block_table, ori_table_stride, cmp_kv, cmp_num_blocks,
                   cmp_block_size, cmp_block_table, cmp_table_stride, cmp_sparse_indices, topk, sinks, metadata,
-                  softmax_scale, cmp_ratio, ori_win_left, scenario, od, num_sms, stage_mask, status, workspace,
-                  workspace_bytes, stream);
+                  softmax_scale, cmp_ratio, ori_win_left, scenario, outs[0], lses ? lses[0] : nullptr, &od, num_sms,
+                  stage_mask, status, workspace, workspace_bytes, stream);
 }

@@ -82,6 +82,8 @@ RANDOM_CASES = [
     dict(ctx=[3000], q_lens=[1], H=16, K=256, bs_ori=64, bs_cmp=64, seed=15),
     dict(ctx=[2000, 1000], q_lens=[3, 4], H=32, K=128, seed=16),
     dict(ctx=[6000, 300], q_lens=[1, 2], H=96, K=384, seed=17),
+    # the CPU-golden decode configuration at its full shape: B4, H16, K256, blocks of 64
+    dict(ctx=[1024, 2048, 3000, 4096], q_lens=[1, 1, 1, 1], H=16, K=256, bs_ori=64, bs_cmp=64, seed=0),
 ]
 
 

@@ -134,6 +134,17 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, 
   }
 }
 
+// Per-warpgroup register limits (every warp of a warpgroup must execute the
+// same one; the increases draw on what the decreases release).
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 // ------------------------------------------------------------------- TMA
 // Programmatic dependent launch: a kernel launched with the programmatic
 // stream-serialization attribute may start before the previous kernel on the

@@ -65,14 +65,25 @@ constexpr int CH = 128;       // KV rows per chunk (MMA M)
 constexpr int NSLAB = 8;      // 64-column slabs per chunk
 constexpr int SLAB_BYTES = CH * 128;  // 16 KB
 constexpr int Q_SLAB_BYTES = HG * 128;  // 8 KB
-// 12 warps, 3 per SM sub-partition (so 168 registers per thread):
-constexpr int kLoaderWarps = 2;         // warps 0-1: cp.async copies of K and V rows
-constexpr int kLoaderThreads = 32 * kLoaderWarps;
+// 16 warps in 4 warpgroups. The launch gives 128 registers per thread; at the
+// top of its role's branch every warp sets its limit (setmaxnreg): the
+// softmax warpgroups 1-2 rise to kRegsSoftmax, warpgroups 0 and 3 drop to
+// kRegsLean, which sums to the launch's 512 x 128 registers exactly.
 constexpr int kMmaWarp = 2;             // warp 2: TMEM owner and MMA issuer
 constexpr int kCoordWarp = 3;           // warp 3: row resolution, runs up to two tiles ahead
 constexpr int kSoftmaxWarp0 = 4;        // warps 4-7: softmax group A (heads 0-31) / epilogue
 constexpr int kSoftmaxWarpB = 8;        // warps 8-11: softmax group B (heads 32-63) / epilogue
-constexpr int kThreads = 32 * 12;
+constexpr int kSoftmaxWarpEnd = 12;
+// warps 0, 1, 12, 13: cp.async copies of K and V rows (the sub-partitions of
+// the MMA and coordinate warps hold no loader; warps 14-15 are idle)
+constexpr int kLoaderWarps = 4;
+constexpr int kLoaderThreads = 32 * kLoaderWarps;
+constexpr int kLoaderLeadWarp = 0;
+__device__ __forceinline__ bool is_loader_warp(int w) { return w < 2 || w == 12 || w == 13; }
+__device__ __forceinline__ int loader_index(int w) { return w < 2 ? w : w - 10; }
+constexpr int kThreads = 32 * 16;
+constexpr int kRegsLaunch = 128, kRegsLean = 96, kRegsSoftmax = 160;
+static_assert(256 * kRegsLean + 256 * kRegsSoftmax == kThreads * kRegsLaunch, "register split");
 constexpr int kTileChunksC = 4;          // chunks per softmax tile (512 rows)
 constexpr int CD = 2 * kTileChunksC;     // depth of the row-coordinate ring (chunks): two tiles
 // A unit of work is one softmax tile of a token, as golden.py tiles the KV
@@ -89,8 +100,15 @@ constexpr float kLn2 = 0.6931471805599453f;
 // (counted over every chunk copy) lives in slot n % kRing. kRing is even and
 // every chunk starts on an even slab number, so the slab pair (2j, 2j+1) of
 // P.V's d-tile j always sits in two adjacent slots (fixed operand stride).
-constexpr int kRing = 6;
-constexpr int kPBuf = 2;                                   // P^T buffers: chunk n uses buffer n % kPBuf
+// The loaders copy a chunk in two halves of kSpan = 4 slabs: one warp
+// instruction copies 512 contiguous bytes of one row (16 B per lane, into 4
+// slabs), so a half occupies 4 consecutive slots and 8 slots keep two halves
+// in flight. Measured on this B200 with 148 CTAs gathering random 1 KB rows:
+// 4 rows x 128 B per instruction fill ~17 B/cycle per SM whatever the warp
+// count or ring depth; 512-byte row spans from 4 warps with 8 slots, ~29.
+constexpr int kSpan = 4;
+constexpr int kRing = 8;
+constexpr int kPBuf = 1;                                   // P^T buffers: chunk n uses buffer n % kPBuf
 constexpr int P_BYTES = CH * 128;                         // one P^T buffer, 16 KB
 constexpr int OFF_Q = 0;
 constexpr int OFF_KV = OFF_Q + NSLAB * Q_SLAB_BYTES;     // 64 KB
@@ -116,7 +134,7 @@ constexpr int MISC_BYTES = M_MW + kTmemMergeMax * 64 * 4;
 constexpr int kFusedMaxT = 512;  // token plans built inside the attention kernel (no plan kernel)
 // fused plan region: TokInfo[kFusedMaxT], units[kFusedMaxT + 1], smax
 constexpr int OFF_PLAN = OFF_MISC + MISC_BYTES;
-constexpr int P_US = kFusedMaxT * 16;
+constexpr int P_US = kFusedMaxT * 8;  // TokInfo[kFusedMaxT]
 constexpr int P_SMAX = P_US + (kFusedMaxT + 1) * 4;
 constexpr int PLAN_BYTES = (P_SMAX + 4 + 15) / 16 * 16;
 constexpr int SMEM_BYTES = OFF_PLAN + PLAN_BYTES + 1024;  // fused plan; + alignment slack
@@ -160,9 +178,12 @@ constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TM_S = 0;     // S^T: kTileChunks slots of 64 columns, chunk n in slot n % kTileChunks
 constexpr uint32_t TM_O = 256;   // O^T: 4 d-tiles of 64 columns
 
+// A query token: its request and causal end position s_g. Its compressed
+// threshold and row count follow from s_g (tok_thr / tok_ncmp).
 struct TokInfo {
-  int b, s_g, n_cmp, thr;
+  int b, s_g;
 };
+static_assert(sizeof(TokInfo) == 8, "fused plan layout");
 
 // Outputs of the head-sharded multi-GPU forward (the GA kernel variants): the
 // call computes heads [h0, h0 + H) of outputs holding H_total heads per
@@ -283,6 +304,15 @@ __device__ __forceinline__ int py_floordiv(int a, int b) {
   if (r != 0 && ((r < 0) != (b < 0))) --q;
   return q;
 }
+// threshold = (s_g + 1) // ratio: compressed ids at or past it are masked
+// (golden.py:41-51); the rows a token scans: min(K, threshold) top-k slots
+// for SCFA, every compressed row below the threshold for CFA, none for SWA
+__device__ __forceinline__ int tok_thr(int s_g, int scenario, int ratio) {
+  return scenario == 1 ? 0 : max(py_floordiv(s_g + 1, ratio), 0);
+}
+__device__ __forceinline__ int tok_ncmp(int thr, int scenario, int K) {
+  return scenario == 3 ? min(K, thr) : (scenario == 2 ? thr : 0);
+}
 
 // ------------------------------------------------------------------ plan
 __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
@@ -340,7 +370,7 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
         s = t - b * p.S;
         act_q = p.cu ? p.cu[b + 1] - p.cu[b] : p.S;
       }
-      TokInfo ti{b, 0, 0, 0};
+      TokInfo ti{b, 0};
       if (s < act_q && b < p.B) {
         const int pid = b * smax + s;
         bool covered = false;
@@ -348,13 +378,8 @@ __global__ void __launch_bounds__(1024, 1) sas_plan_kernel(PlanParams p) {
           covered |= (s_en[i] != 0) && pid >= s_lin[i][0] && pid < s_lin[i][1];
         const int act_kv = p.seqused_kv[b];
         const int s_g = act_kv - act_q + s;
-        const int thr = max(py_floordiv(s_g + 1, p.ratio), 0);
-        int n_cmp = 0;
-        if (p.scenario == 3) n_cmp = min(p.K, thr);
-        else if (p.scenario == 2) n_cmp = thr;
+        const int n_cmp = tok_ncmp(tok_thr(s_g, p.scenario, p.ratio), p.scenario, p.K);
         ti.s_g = s_g;
-        ti.n_cmp = n_cmp;
-        ti.thr = thr;
         if (covered) units = token_tiles(p.n_win_chunks, n_cmp);
       }
       p.tok[t] = ti;
@@ -504,13 +529,13 @@ struct TileIter {
     k = 0;
     sg.ce = 0;
   }
-  __device__ bool next(Tile& tl, const TokInfo* tokp, int n_win_chunks) {
+  __device__ bool next(Tile& tl, const TokInfo* tokp, int n_win_chunks, int scenario, int ratio, int K) {
     if (!started || k >= sg.ce) {
       if (!wk.next(sg)) return false;
       if (started) ++seg;
       started = true;
       k = sg.cb;
-      n_cmp = tokp[sg.t].n_cmp;
+      n_cmp = tok_ncmp(tok_thr(tokp[sg.t].s_g, scenario, ratio), scenario, K);
     }
     int c1;
     tile_chunks(k, n_win_chunks, n_cmp, tl.c0, c1);
@@ -1288,16 +1313,12 @@ __device__ void fused_plan(const FwdParams& p, TokInfo* s_tok, int32_t* s_us, in
   for (int w = 0; w < kW; ++w) smax = max(smax, s_wsum[w]);
   // one thread per request (TND) or per token (BSND): no per-token search
   auto plan_token = [&](int t, int b, int s, int act_q) {
-    TokInfo ti{b, 0, 0, 0};
+    TokInfo ti{b, 0};
     int units = 0;
     if (s < act_q && b < p.B) {
       const int s_g = p.seqused_kv[b] - act_q + s;
-      const int thr = max(py_floordiv(s_g + 1, p.ratio), 0);
-      const int n_cmp = p.scenario == 3 ? min(p.K, thr) : (p.scenario == 2 ? thr : 0);
       ti.s_g = s_g;
-      ti.n_cmp = n_cmp;
-      ti.thr = thr;
-      units = token_tiles(p.n_win_chunks, n_cmp);
+      units = token_tiles(p.n_win_chunks, tok_ncmp(tok_thr(s_g, p.scenario, p.ratio), p.scenario, p.K));
     }
     s_tok[t] = ti;
     s_us[t] = units;
@@ -1455,7 +1476,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   if (TRACE && tid == 0) ev(15);
 
+  // Register split: each role sets its limit at the top of its branch, so the
+  // compiler allocates every branch under that limit; all warps of a
+  // warpgroup execute the same value (warps 0-3 and 12-15: kRegsLean, warps
+  // 4-11: kRegsSoftmax).
   if (warp == kCoordWarp) {
+    sas::setmaxnreg_dec<kRegsLean>();
     // =============================== row resolution, up to CD chunks ahead
     // Lane l resolves rows l, l+32, l+64, l+96 of every chunk through the
     // block tables (kernel.py:285-401, 686-766) and writes the pool row (or
@@ -1466,17 +1492,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     it.init(usp, *reinterpret_cast<const RangeInfo*>(misc + M_RANGE));
     Tile tl;
     TokInfo ti{};
+    int ti_thr = 0, ti_ncmp = 0;
     bool stopped = false, ok = true;
-    while (ok && it.next(tl, tokp, p.n_win_chunks)) {
+    while (ok && it.next(tl, tokp, p.n_win_chunks, p.scenario, p.ratio, p.K)) {
       const long long tc0 = tracing ? clock64() : 0;
       if (tl.first) {
         ti = tokp[tl.t];
+        ti_thr = tok_thr(ti.s_g, p.scenario, p.ratio);
+        ti_ncmp = tok_ncmp(ti_thr, p.scenario, p.K);
         // the compressed scan stops at the first -1 (golden.py:55-56): a range
         // that starts inside a token looks for one in the slots before it
         stopped = false;
         const int cmp_c0 = max(tl.c0 - p.n_win_chunks, 0);
         if (p.scenario == 3 && cmp_c0 > 0) {
-          const int lim = min(cmp_c0 * CH, ti.n_cmp);
+          const int lim = min(cmp_c0 * CH, ti_ncmp);
           const int32_t* ip = p.idx + (size_t)tl.t * p.K;
           int neg = 0;
           for (int e = lane; e < lim; e += 32) neg |= (ip[e] == -1);
@@ -1512,7 +1541,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             const int e = e0 + j * CH + k * 32 + lane;
-            val[j][k] = j < tl.nch && e < ti.n_cmp;
+            val[j][k] = j < tl.nch && e < ti_ncmp;
             coord[j][k] = e;  // the compressed id, until resolved
             if (p.scenario == 3) coord[j][k] = val[j][k] ? p.idx[(size_t)tl.t * p.K + e] : 0;
           }
@@ -1527,14 +1556,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              val[j][k] = val[j][k] && !stopped && k * 32 + lane < cf && coord[j][k] >= 0 && coord[j][k] < ti.thr;
+              val[j][k] = val[j][k] && !stopped && k * 32 + lane < cf && coord[j][k] >= 0 && coord[j][k] < ti_thr;
             stopped = stopped || (j < tl.nch && cf < CH);
           }
         } else {
 #pragma unroll
           for (int j = 0; j < kTileChunks; ++j)
 #pragma unroll
-            for (int k = 0; k < 4; ++k) val[j][k] = val[j][k] && coord[j][k] < ti.thr;
+            for (int k = 0; k < 4; ++k) val[j][k] = val[j][k] && coord[j][k] < ti_thr;
         }
 #pragma unroll
         for (int j = 0; j < kTileChunks; ++j)
@@ -1590,39 +1619,44 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp < kLoaderWarps) {
+  } else if (is_loader_warp(warp)) {
+    sas::setmaxnreg_dec<kRegsLean>();
     // =============================== loaders: K rows, then V rows, per tile
     // The copies run in the MMA's consumption order (K of every chunk of a
     // tile, then V of every chunk) and block only on ring slots, which QK^T
     // and P.V free as they read them.
-    const int lw = warp;  // rows [64*lw, 64*lw+64) of every chunk
-    const int sub = lane >> 3, c16 = lane & 7;
+    const int lw = loader_index(warp);  // rows [32*lw, 32*lw+32) of every chunk
+    const int sl = lane >> 3, c16 = lane & 7;  // slab of the half, 16-byte piece of its 128 bytes
+    const bool lead = tid == kLoaderLeadWarp * 32;
     const uint32_t kv_base = sas::smem_u32(smem + OFF_KV);
     uint32_t sc = 0;  // ring slabs filled so far
     const uint32_t q_bytes = (uint32_t)NSLAB * p.q_box_h * 128;
     bool ok = true;
     // copy the 128 rows of chunk-slot `cslot` (pool rows resolved by the
-    // coordinate warp) into the ring: one 16 KB slab per mbarrier
+    // coordinate warp) into the ring, in two halves of kSpan slabs:
+    // instruction i of a half copies 512 contiguous bytes of row 32*lw + i,
+    // lane l the 16 B piece c16 of slab sl; every lane then arrives on the
+    // half's slab barriers
     auto load_chunk = [&](uint32_t cslot, bool is_win) -> bool {
-      int crw[16];  // rows this lane copies: 4 rows x 8 lanes x 16 B per instruction, 16 times
-#pragma unroll
-      for (int i = 0; i < 16; ++i) crw[i] = coords[cslot * CH + lw * 64 + 4 * i + sub];
+      const int myrow = coords[cslot * CH + lw * 32 + lane];  // lane i holds row 32*lw + i
       const uint8_t* pool = is_win ? p.ori_kv : p.cmp_kv;
-      for (int s = 0; s < NSLAB; ++s, ++sc) {
-        const uint32_t slot = sc % kRing;
-        if (!twait(&bars[B_EMPTY + slot], ((sc / kRing) & 1) ^ 1, abort_flag, p.status, 3, tracing,
-                   tr[TR_P_WAIT_EMPTY]))
-          return false;
-        const uint32_t slab = kv_base + slot * SLAB_BYTES;
+      for (int h = 0; h < NSLAB / kSpan; ++h, sc += kSpan) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int rl = 4 * i + sub;
-          const uint32_t dst = slab + (lw * 64 + rl) * 128 + ((c16 ^ (rl & 7)) << 4);
-          const bool v = crw[i] >= 0;
-          const uint8_t* src = pool + (size_t)(v ? crw[i] : 0) * (D * 2) + s * 128 + c16 * 16;
-          cp_async16(dst, src, v ? 16u : 0u);
+        for (int j = 0; j < kSpan; ++j)
+          if (!twait(&bars[B_EMPTY + (sc + j) % kRing], (((sc + j) / kRing) & 1) ^ 1, abort_flag, p.status, 3,
+                     tracing, tr[TR_P_WAIT_EMPTY]))
+            return false;
+        const uint32_t slab = kv_base + ((sc + sl) % kRing) * SLAB_BYTES;
+        const uint8_t* src0 = pool + (h * kSpan + sl) * 128 + c16 * 16;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const int row = __shfl_sync(0xffffffffu, myrow, i);
+          const int rl = lw * 32 + i;
+          const bool v = row >= 0;
+          cp_async16(slab + rl * 128 + ((c16 ^ (rl & 7)) << 4), src0 + (size_t)(v ? row : 0) * (D * 2), v ? 16u : 0u);
         }
-        cp_async_arrive(&bars[B_FULL + slot]);
+#pragma unroll
+        for (int j = 0; j < kSpan; ++j) cp_async_arrive(&bars[B_FULL + (sc + j) % kRing]);
       }
       return true;
     };
@@ -1639,7 +1673,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t n = st.nk++;
         const int2 ci = cinfo[n % CD];
         if (ci.x & CF_SEG_FIRST) {
-          if (tid == 0) {
+          if (lead) {
             if (!twait(&bars[B_QEMPTY], (seg_i & 1) ^ 1, abort_flag, p.status, 1, tracing, tr[TR_P_WAIT_EMPTY])) {
               ok = false;
             } else {
@@ -1652,12 +1686,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++seg_i;
         }
         if (ok) ok = load_chunk(n % CD, ci.x & CF_WIN);
-        if (TRACE && tid == 0 && n == 0) ev(5);
-        if (TRACE && tid == 0 && n == 4) ev(6);
+        if (TRACE && lead && n == 0) ev(5);
+        if (TRACE && lead && n == 4) ev(6);
       } else {  // V rows: the K rows again, mostly from L2
         const uint32_t n = st.nv++;
         ok = load_chunk(n % CD, cinfo[n % CD].x & CF_WIN);
-        if (TRACE && tid == 0 && n == 0) ev(4);
+        if (TRACE && lead && n == 0) ev(4);
         __syncwarp();
         if (lane == 0) sas::mbar_arrive(&bars[B_CEMPTY + n % CD]);
       }
@@ -1665,8 +1699,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // nothing may still be landing in shared memory when the CTA exits (an
     // aborted CTA leaves the loop with copies in flight)
     asm volatile("cp.async.wait_all;" ::: "memory");
-    if (tid == 0 && q_loads > 0) sas::mbar_wait_drain(&bars[B_QFULL], (q_loads - 1) & 1, SAS_WAIT_LIMIT_NS);
+    if (lead && q_loads > 0) sas::mbar_wait_drain(&bars[B_QFULL], (q_loads - 1) & 1, SAS_WAIT_LIMIT_NS);
   } else if (warp == kMmaWarp) {
+    sas::setmaxnreg_dec<kRegsLean>();
     // =============================== MMA issuer
     // Per tile: S^T of every chunk into its own TMEM slot as the K rows land,
     // then, per chunk, O^T += V^T P^T as the V rows land and P is ready.
@@ -1783,7 +1818,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       sas::mbar_wait_drain(&bars[B_DRAIN], 0, SAS_WAIT_LIMIT_NS);
     }
     __syncwarp();
-  } else if (warp >= kSoftmaxWarp0) {
+  } else if (warp >= kSoftmaxWarp0 && warp < kSoftmaxWarpEnd) {
+    sas::setmaxnreg_inc<kRegsSoftmax>();
     // =============================== softmax groups A (warps 4-7, heads 0-31)
     // and B (warps 8-11, heads 32-63) / epilogue
     const int quad = warp & 3;  // TMEM lane quadrant of this warp
@@ -1802,7 +1838,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool trace_me = tracing && half == 0;
     unsigned long long trb[TR_NSLOTS];
     unsigned long long* trp = half == 0 ? tr : trb;
-    while (ok && it.next(tl, tokp, p.n_win_chunks)) {
+    while (ok && it.next(tl, tokp, p.n_win_chunks, p.scenario, p.ratio, p.K)) {
       for (int i = 0; ok && i < tl.nch; ++i)  // the tile's validity masks
         ok = twait(&bars[B_CFULL + (tl.g0 + i) % CD], ((tl.g0 + i) / CD) & 1, abort_flag, p.status, 8, trace_me,
                    trp[TR_S_WAIT_MASK]);
@@ -1839,11 +1875,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (FUSED && ok)
       zero_uncovered<DT, GA>(p, G, usp, tokp, reinterpret_cast<const int*>(smem + OFF_PLAN + P_SMAX),
                          *reinterpret_cast<const RangeInfo*>(misc + M_RANGE), g, abort_flag);
+  } else {
+    sas::setmaxnreg_dec<kRegsLean>();  // warps 14-15: idle
   }
 
   if (TRACE) {
     unsigned long long* tp = p.trace + (size_t)blockIdx.x * TR_NSLOTS;
-    if (tid == 0) {
+    if (tid == kLoaderLeadWarp * 32) {
       tp[TR_P_WAIT_EMPTY] = tr[TR_P_WAIT_EMPTY];
       tp[TR_P_WAIT_MASK] = tr[TR_P_WAIT_MASK];
     } else if (tid == kCoordWarp * 32) {

@@ -23,14 +23,15 @@
 //    rounded at the same points as the reference; since the max needs every
 //    score of the tile first, each 128-row chunk is copied twice: K(n) for
 //    the scores, then V(n) (the same rows, mostly from L2) for P.V.
-//    Per CTA, warp-specialised (12 warps):
+//    Per CTA, warp-specialised (16 warps; warps 14-15 idle):
 //      warp 3   rows: resolves window positions / top-k ids through the
 //               block tables (kernel.py:285-401, 686-766) a tile at a time,
 //               and publishes per chunk the pool rows, a 128-bit validity
 //               mask and the chunk's flags into an 8-deep ring.
-//      warps 0-1 loaders: 16-byte cp.async of the rows into 16 KB slabs
+//      warps 0, 1, 12, 13 loaders: cp.async of the rows into 16 KB slabs
 //               (128B-swizzled K-major; masked rows zero-filled without a
-//               read), in the copy-stream order shared with the MMA thread.
+//               read), one warp instruction = 512 contiguous bytes of one
+//               row, in the copy-stream order shared with the MMA thread.
 //      warp 2   MMA issuer (one thread) and TMEM owner: transposed attention
 //               so the KV rows fill the M=128 datapath and the 64 heads are N:
 //                 S^T[128 x 64]  = K[128 x 512] . Q^T          (K-major A and B)

@@ -3,8 +3,8 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C5] [--impl ours|reference]
 
 One step = one call of the op over one batch: the GPU scheduler
-(SparseAttnSharedkvMetadata) plus the fused attention (plan, attention,
-split-KV combine), replayed from a CUDA graph, with the inputs resident in
+(SparseAttnSharedkvMetadata) plus the attention (a plan kernel above 512
+tokens, then the fused attention kernel), replayed from a CUDA graph, with the inputs resident in
 HBM. L2 is flushed (a 512 MB write) between timed steps, untimed. Each step
 is timed with CUDA events on the launching stream; under torchrun every rank
 runs its own batch (request-parallel, weak scaling: no collective on the data

@@ -37,3 +37,13 @@ def test_library_is_sm100a_only():
     from dsv4_b200 import build
 
     assert "arch=compute_100a,code=sm_100a" in build.ARCH
+
+
+def test_bench_fused_plan_threshold_matches_kernel():
+    """bench.py counts launches per step from the fused-plan threshold; it must
+    be the attention kernel's own (kFusedMaxT in csrc/sas_fwd.cu)."""
+    import bench
+
+    src = open(os.path.join(ROOT, "dsv4_b200", "csrc", "sas_fwd.cu")).read()
+    m = re.search(r"constexpr int kFusedMaxT = (\d+);", src)
+    assert m and int(m.group(1)) == bench.FUSED_PLAN_MAX_TOKENS
